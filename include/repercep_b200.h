@@ -1,0 +1,130 @@
+/*
+ * repercep_b200.h — C ABI of librepercep_b200.so, the B200 (sm_100a) FP8
+ * attention hot path of repercep-runtime.
+ *
+ * Conventions (every entry point):
+ *   - plain pointers and sizes, no framework types; device pointers are CUDA
+ *     device memory owned by the caller; `stream` is a cudaStream_t (NULL =
+ *     legacy default stream);
+ *   - asynchronous and stream-ordered; no host synchronisation, no device
+ *     allocation;
+ *   - return RP_OK (0) or a negative rp_status; the message of the calling
+ *     thread's last failure is available from rp_last_error();
+ *   - bf16 inputs/outputs are addressed by element strides with the head
+ *     dimension unit-stride, so (B,H,S,D) and (B,S,H,D) tensors both work
+ *     without a transposing copy;
+ *   - e4m3 tensors produced here are contiguous (B*H, S, D);
+ *   - scale tensors are fp32 dequant multipliers: (B*H) for RP_SCALE_PER_BH,
+ *     (B*H, ceil(S/128)) for RP_SCALE_PER_BLOCK128.
+ *
+ * Reference interfaces replaced (paths inside miteshs/repercep-runtime):
+ *   rp_quant_fp8_e4m3      <- _per_bh_scale + _quantize,
+ *                             kernels/triton_kernels/fp8_flash_attn_hopper.py:374-398
+ *   rp_attn_fp8_fwd        <- _fp8_flash_attn_fwd_impl launch inside
+ *                             fp8_flash_attention, fp8_flash_attn_hopper.py:432-586
+ *   rp_attn_fp8_fwd_chunked<- (no reference counterpart: the reference refuses
+ *                             context parallelism, attention/diffusers_backend.py:199-212)
+ *   rp_attn_fp8_prefix_decode <- (no reference kernel: the reference expands the
+ *                             prompt per candidate, scripts/run_vla_openvla_gpu.py:174-186)
+ */
+#ifndef REPERCEP_B200_H_
+#define REPERCEP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RP_ABI_VERSION 1
+
+typedef enum rp_status {
+  RP_OK = 0,
+  RP_ERR_INVALID = -1,     /* bad argument (null pointer, negative size, ...) */
+  RP_ERR_UNSUPPORTED = -2, /* shape or mode this build does not implement */
+  RP_ERR_ALIGN = -3,       /* pointer or stride alignment the TMA unit rejects */
+  RP_ERR_ARCH = -4,        /* current device is not sm_100 */
+  RP_ERR_CUDA = -5,        /* CUDA runtime/driver error (see rp_last_error) */
+  RP_ERR_WORKSPACE = -6    /* workspace missing or too small */
+} rp_status;
+
+typedef enum rp_scale_mode {
+  RP_SCALE_PER_BH = 0,       /* one scale per (b,h): the reference's semantics */
+  RP_SCALE_PER_BLOCK128 = 1  /* one scale per 128-token block of each (b,h) */
+} rp_scale_mode;
+
+typedef enum rp_p_mode {
+  RP_P_E4M3 = 0,      /* P rounded once to e4m3 (reference precision) */
+  RP_P_E4M3_HILO = 1  /* P split into e4m3 hi + lo planes, two PV MMAs */
+} rp_p_mode;
+
+/* ABI version compiled into the library (RP_ABI_VERSION). */
+int rp_abi_version(void);
+
+/* NUL-terminated message of the calling thread's last failed call ("" if none). */
+const char* rp_last_error(void);
+
+/* Device status word written by kernels whose internal pipeline timed out
+ * (0 = healthy).  Reads it for the current device (synchronises the device);
+ * when `reset` is non-zero it is cleared afterwards.  Diagnostic only. */
+int rp_device_status(int* status, int reset);
+
+/* Workspace bytes rp_quant_fp8_e4m3 needs (0 for RP_SCALE_PER_BLOCK128). */
+int rp_quant_workspace_bytes(int num_tensors, int B, int H, int S, int D, int scale_mode,
+                             size_t* bytes);
+
+/* Quantise `num_tensors` (1..3) bf16 tensors of one shape (B,H,S,D) to e4m3.
+ *   x[i]       bf16 input, element (b,h,s,d) at x[i] + b*strides[4i] +
+ *              h*strides[4i+1] + s*strides[4i+2] + d (strides[4i+3] must be 1)
+ *   out[i]     e4m3 output, contiguous (B*H, S, D)
+ *   scales[i]  fp32 dequant scales (layout per scale_mode)
+ * Replaces _per_bh_scale/_quantize (fp8_flash_attn_hopper.py:374-398);
+ * bytes and scales are bit-identical to them for RP_SCALE_PER_BH. */
+int rp_quant_fp8_e4m3(int num_tensors, const void* const* x, const int64_t* strides, int B, int H,
+                      int S, int D, int scale_mode, void* const* out, float* const* scales,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* FP8 attention forward, non-causal or causal (top-left aligned mask, as the
+ * reference's offs_m >= offs_n).  q8 (B*H, Sq, D), k8/v8 (B*H, Skv, D) e4m3
+ * contiguous; qs/ks/vs dequant scales in `scale_mode` layout; out bf16
+ * (B,H,Sq,D) addressed by out_strides[4] (elements; last must be 1).
+ * sm_scale <= 0 selects 1/sqrt(D).  D must be 128.
+ * Replaces the kernel launch of fp8_flash_attention (fp8_flash_attn_hopper.py:432-586). */
+int rp_attn_fp8_fwd(const void* q8, const void* k8, const void* v8, const float* qs,
+                    const float* ks, const float* vs, int scale_mode, int B, int H, int Sq,
+                    int Skv, int D, float sm_scale, int causal, int p_mode, void* out,
+                    const int64_t* out_strides, void* stream);
+
+/* Context-parallel variant: K/V arrive as `n_chunks` chunks (one per rank),
+ * laid out (n_chunks, B*H, chunk_rows, D) e4m3; every chunk holds chunk_rows
+ * valid rows except the last, which holds last_rows.  chunk_rows must be a
+ * multiple of 128 when n_chunks > 1.  Scales are per 128-row block:
+ * (n_chunks, B*H, ceil(chunk_rows/128)).  q8/qs as rp_attn_fp8_fwd with
+ * RP_SCALE_PER_BLOCK128.  Non-causal. */
+int rp_attn_fp8_fwd_chunked(const void* q8, const void* k8, const void* v8, const float* qs,
+                            const float* ks, const float* vs, int B, int H, int Sq,
+                            int n_chunks, int chunk_rows, int last_rows, int D, float sm_scale,
+                            int p_mode, void* out, const int64_t* out_strides, void* stream);
+
+/* Shared-prefix candidate decode.  C candidates x T new tokens per head:
+ *   q8   (H, C*T, D)   e4m3, qs (H, ceil(C*T/128)) per-block scales
+ *   kp8, vp8 (H, P, D) e4m3 shared prefix, kps/vps (H, ceil(P/128))
+ *   kx8, vx8 (H, C*T, D) e4m3 per-candidate suffix, kxs/vxs (H, ceil(C*T/128))
+ *   out  bf16 (C*T, H, D) addressed by out_strides[3] = {token, head, d}
+ * Candidate c's token i attends to the whole prefix and to its own suffix
+ * tokens 0..i.  Every query tile reads each prefix K/V tile once; 128 % T
+ * must be 0.  (No reference kernel: the reference duplicates the prefix per
+ * candidate, scripts/run_vla_openvla_gpu.py:174-186.) */
+int rp_attn_fp8_prefix_decode(const void* q8, const void* kp8, const void* vp8,
+                              const void* kx8, const void* vx8, const float* qs,
+                              const float* kps, const float* vps, const float* kxs,
+                              const float* vxs, int C, int T, int P, int H, int D,
+                              float sm_scale, int p_mode, void* out,
+                              const int64_t* out_strides, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REPERCEP_B200_H_ */

@@ -1,0 +1,596 @@
+// FP8 (e4m3) flash-attention forward for sm_100a: TMA-fed, tcgen05/TMEM,
+// warp-specialised.  Restates the algorithm of the reference's fused kernel
+// (kernels/triton_kernels/fp8_flash_attn_hopper.py:197-338): per-tile
+// S = Q K^T in fp32 scaled by softmax_scale * q_scale * k_scale, an online
+// softmax, P quantised to e4m3 against a fixed 448 range (:322), O += P V
+// scaled by v_scale / 448 (:323-327), O /= l (:332).
+//
+// CTA layout (NQ query tiles of 128 rows share each K/V tile):
+//   warps [0, 4*NQ)   softmax warpgroups, warpgroup t owns query tile t; a
+//                     thread owns one query row == one TMEM lane
+//   warp  4*NQ        TMA producer (Q once, then a ring of K and V tiles)
+//   warp  4*NQ + 1    MMA issuer (one thread issues every tcgen05.mma)
+// TMEM: S[t] at columns [128 t, 128 t + 128), O[t] at [128 (NQ + t), ...).
+// SMEM (1024-byte aligned, 128-byte swizzle everywhere):
+//   Q[NQ] | K[3] | V[3] | P[NQ][PBUF] (hi [+ lo] planes) | mbarriers
+// Operand majors: Q, K, P are K-major; V is MN-major (its natural [kv][d]
+// layout), which tcgen05 accepts for e4m3.
+//
+// Scales are generalised from the reference's one-per-(b,h) to any grid of
+// 128-row blocks: k_scale / v_scale may change per K/V tile.  v_scale is
+// folded into P: P' = e4m3(p * 448 * sv_j / sv_max) so one TMEM accumulator
+// serves every tile, and the epilogue multiplies by sv_max / 448 / l.
+//
+// PMODE 0: P is one e4m3 plane (the reference's precision).
+// PMODE 1: P is split into e4m3 hi + lo planes and PV runs twice, which
+//          removes almost all of the P rounding error.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include <atomic>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace rp {
+namespace {
+
+constexpr int kTile = 128;
+constexpr int kTileBytes = kTile * kTile;
+constexpr int kKSt = 3;
+constexpr int kVSt = 3;
+
+enum : int {
+  kErrWaitQ = 0x101,
+  kErrWaitK = 0x102,
+  kErrWaitV = 0x103,
+  kErrWaitKEmpty = 0x104,
+  kErrWaitVEmpty = 0x105,
+  kErrWaitS = 0x106,
+  kErrWaitSFree = 0x107,
+  kErrWaitP = 0x108,
+  kErrWaitO = 0x109,
+  kErrWaitEpi = 0x10A,
+};
+
+template <int NQ, int PMODE>
+struct Cfg {
+  static constexpr int kSoftmaxWarps = 4 * NQ;
+  static constexpr int kTmaWarp = kSoftmaxWarps;
+  static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+  static constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
+  static constexpr int kPBuf = (PMODE == 0) ? 2 : 1;
+  static constexpr int kPParts = (PMODE == 0) ? 1 : 2;
+  static constexpr int kTmemCols = (NQ == 2) ? 512 : 256;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + NQ * kTileBytes;
+  static constexpr int kOffV = kOffK + kKSt * kTileBytes;
+  static constexpr int kOffP = kOffV + kVSt * kTileBytes;
+  static constexpr int kPStride = kPParts * kTileBytes;
+  static constexpr int kOffBar = kOffP + NQ * kPBuf * kPStride;
+  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 5 * NQ + 1;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct Bars {
+  uint64_t *q_full, *k_full, *k_empty, *v_full, *v_empty;
+  uint64_t *s_full, *s_free, *p_full, *o_done, *epi, *fin;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+};
+
+template <int NQ>
+__device__ __forceinline__ Bars carve_bars(uint8_t* base) {
+  Bars b;
+  uint64_t* p = reinterpret_cast<uint64_t*>(base);
+  b.q_full = p;
+  b.k_full = b.q_full + 1;
+  b.k_empty = b.k_full + kKSt;
+  b.v_full = b.k_empty + kKSt;
+  b.v_empty = b.v_full + kVSt;
+  b.s_full = b.v_empty + kVSt;
+  b.s_free = b.s_full + NQ;
+  b.p_full = b.s_free + NQ;
+  b.o_done = b.p_full + NQ;
+  b.epi = b.o_done + NQ;
+  b.fin = b.epi + NQ;
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.fin + 1);
+  b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
+  return b;
+}
+
+// Lane 0 waits, the warp follows.  Keeps every .sync.aligned tcgen05
+// instruction after the wait warp-convergent even when the wait aborts.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, status, code) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+// Time-bounded wait that ignores the abort flag: used to drain in-flight
+// asynchronous work before the CTA releases its shared memory and TMEM.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitLimitCycles / 4) return;
+  }
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
+// Residual of four values after their e4m3 rounding in `packed`, re-packed.
+__device__ __forceinline__ uint32_t pack_e4m3x4_residual(uint32_t packed, float a, float b,
+                                                         float c, float d) {
+  const __half2_raw h01 =
+      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(packed & 0xFFFFu), __NV_E4M3);
+  const __half2_raw h23 =
+      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(packed >> 16), __NV_E4M3);
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  return pack_e4m3x4(a - f01.x, b - f01.y, c - f23.x, d - f23.y);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Which K/V tile step j reads: chunk c, tile t within the chunk, valid rows.
+__device__ __forceinline__ void step_info(const AttnKernelParams& p, int j, int& c, int& t,
+                                          int& valid, bool& extra) {
+  if (p.has_extra && j == p.n_main_tiles) {
+    extra = true;
+    c = 0;
+    t = 0;
+    valid = kTile;
+    return;
+  }
+  extra = false;
+  c = j / p.tiles_per_chunk;
+  t = j - c * p.tiles_per_chunk;
+  const int len = (c == p.n_chunks - 1) ? p.last_len : p.chunk_len;
+  valid = min(kTile, len - t * kTile);
+}
+
+// ------------------------------------------------------------ TMA producer
+template <int NQ, int PMODE>
+__device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                         const CUtensorMap* tm_kx, const CUtensorMap* tm_vx,
+                         const AttnKernelParams& p, const Bars& bar, uint8_t* smem, int n_steps) {
+  using C = Cfg<NQ, PMODE>;
+  const int bh = blockIdx.y;
+  const int qt0 = blockIdx.x * NQ;
+  mbar_arrive_expect_tx(bar.q_full, NQ * kTileBytes);
+#pragma unroll
+  for (int t = 0; t < NQ; ++t)
+    tma_load_4d(smem + C::kOffQ + t * kTileBytes, tm_q, bar.q_full, 0, (qt0 + t) * kTile, bh, 0);
+
+  int nk = 0, nv = 0;
+  bool ok = true;
+  for (int j = 0; j < n_steps && ok; ++j) {
+    int c, t, valid;
+    bool extra;
+    step_info(p, j, c, t, valid, extra);
+    const int ks = j % kKSt, ku = j / kKSt;
+    if (ku > 0 && !mbar_wait(bar.k_empty + ks, (ku - 1) & 1, bar.abort_flag, p.status,
+                             kErrWaitKEmpty)) {
+      ok = false;
+      break;
+    }
+    mbar_arrive_expect_tx(bar.k_full + ks, kTileBytes);
+    if (extra)
+      tma_load_4d(smem + C::kOffK + ks * kTileBytes, tm_kx, bar.k_full + ks, 0, qt0 * kTile, bh, 0);
+    else
+      tma_load_4d(smem + C::kOffK + ks * kTileBytes, tm_k, bar.k_full + ks, 0, t * kTile, bh, c);
+    ++nk;
+    const int vs = j % kVSt, vu = j / kVSt;
+    if (vu > 0 && !mbar_wait(bar.v_empty + vs, (vu - 1) & 1, bar.abort_flag, p.status,
+                             kErrWaitVEmpty)) {
+      ok = false;
+      break;
+    }
+    mbar_arrive_expect_tx(bar.v_full + vs, kTileBytes);
+    if (extra)
+      tma_load_4d(smem + C::kOffV + vs * kTileBytes, tm_vx, bar.v_full + vs, 0, qt0 * kTile, bh, 0);
+    else
+      tma_load_4d(smem + C::kOffV + vs * kTileBytes, tm_v, bar.v_full + vs, 0, t * kTile, bh, c);
+    ++nv;
+  }
+  if (!ok) {
+    // Abort: let every load already issued land before shared memory goes away.
+    mbar_drain(bar.q_full, 0);
+    for (int s = 0; s < kKSt; ++s)
+      if (s < nk) mbar_drain(bar.k_full + s, ((nk - 1 - s) / kKSt) & 1);
+    for (int s = 0; s < kVSt; ++s)
+      if (s < nv) mbar_drain(bar.v_full + s, ((nv - 1 - s) / kVSt) & 1);
+  }
+}
+
+// -------------------------------------------------------------- MMA issuer
+template <int NQ, int PMODE>
+__device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& bar,
+                                         uint32_t sbase, uint32_t tmem, int i) {
+  using C = Cfg<NQ, PMODE>;
+  constexpr uint32_t idesc_pv = make_idesc_e4m3(128, 128, 0, 1);
+  const int vsl = i % kVSt;
+  if (!mbar_wait(bar.v_full + vsl, (i / kVSt) & 1, bar.abort_flag, p.status, kErrWaitV))
+    return false;
+  const uint64_t vd = make_sw128_desc(sbase + C::kOffV + vsl * kTileBytes, kTileBytes, 1024);
+#pragma unroll
+  for (int t = 0; t < NQ; ++t) {
+    if (!mbar_wait(bar.p_full + t, i & 1, bar.abort_flag, p.status, kErrWaitP)) return false;
+    tc_fence_after();
+    const int pb = (C::kPBuf == 2) ? (i & 1) : 0;
+    const uint32_t paddr = sbase + C::kOffP + (t * C::kPBuf + pb) * C::kPStride;
+    const uint64_t pd = make_sw128_desc(paddr, 16, 1024);
+    const uint32_t d_tmem = tmem + (NQ + t) * kTile;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      mma_f8(d_tmem, pd + 2 * k, vd + 256 * k, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+    if constexpr (PMODE == 1) {
+      const uint64_t pl = make_sw128_desc(paddr + kTileBytes, 16, 1024);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mma_f8(d_tmem, pl + 2 * k, vd + 256 * k, idesc_pv, 1u);
+    }
+    mma_commit(bar.o_done + t);
+  }
+  mma_commit(bar.v_empty + vsl);
+  return true;
+}
+
+template <int NQ, int PMODE>
+__device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* smem,
+                           uint32_t tmem, int n_steps) {
+  using C = Cfg<NQ, PMODE>;
+  constexpr uint32_t idesc_qk = make_idesc_e4m3(128, 128, 0, 0);
+  const uint32_t sbase = smem_u32(smem);
+  bool ok = mbar_wait(bar.q_full, 0, bar.abort_flag, p.status, kErrWaitQ);
+  for (int j = 0; ok && j < n_steps; ++j) {
+    const int ks = j % kKSt;
+    if (!mbar_wait(bar.k_full + ks, (j / kKSt) & 1, bar.abort_flag, p.status, kErrWaitK)) {
+      ok = false;
+      break;
+    }
+    const uint64_t kd = make_sw128_desc(sbase + C::kOffK + ks * kTileBytes, 16, 1024);
+#pragma unroll
+    for (int t = 0; t < NQ; ++t) {
+      if (j > 0 &&
+          !mbar_wait(bar.s_free + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitSFree)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t qd = make_sw128_desc(sbase + C::kOffQ + t * kTileBytes, 16, 1024);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma_f8(tmem + t * kTile, qd + 2 * k, kd + 2 * k, idesc_qk, k > 0 ? 1u : 0u);
+      mma_commit(bar.s_full + t);
+    }
+    if (!ok) break;
+    mma_commit(bar.k_empty + ks);
+    if (j > 0) ok = issue_pv<NQ, PMODE>(p, bar, sbase, tmem, j - 1);
+  }
+  if (ok && n_steps > 0) issue_pv<NQ, PMODE>(p, bar, sbase, tmem, n_steps - 1);
+  // Everything this thread issued must finish before TMEM is released.
+  mma_commit(bar.fin);
+  mbar_drain(bar.fin, 0);
+}
+
+// ----------------------------------------------------------------- softmax
+template <int NQ, int PMODE>
+__device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
+                           uint8_t* smem, uint32_t tmem, int n_steps) {
+  using C = Cfg<NQ, PMODE>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = warp >> 2, wq = warp & 3;
+  const int row = wq * 32 + lane;
+  const int bh = blockIdx.y;
+  const int q_tile = blockIdx.x * NQ + t;
+  const int q_tile_c = min(q_tile, p.n_q_tiles - 1);
+  const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+  const uint32_t tS = tmem + lane_base + t * kTile;
+  const uint32_t tO = tmem + lane_base + (NQ + t) * kTile;
+  uint8_t* pbase = smem + C::kOffP + t * C::kPBuf * C::kPStride;
+
+  const float sq = p.qs[bh * p.qs_bh + q_tile_c * p.qs_blk];
+
+  // Largest V scale this CTA meets (positive floats order like their bits).
+  uint32_t vbits = 0;
+  for (int j = lane; j < p.n_main_tiles; j += 32) {
+    int c, tt, valid;
+    bool extra;
+    step_info(p, j, c, tt, valid, extra);
+    vbits = max(vbits, __float_as_uint(p.vs[c * p.kv_chunk + bh * p.kv_bh + tt * p.kv_blk]));
+  }
+  if (p.has_extra && lane == 0)
+    vbits = max(vbits, __float_as_uint(p.vsx[bh * p.kvx_bh + q_tile_c * p.kvx_blk]));
+  vbits = __reduce_max_sync(0xffffffffu, vbits);
+  const float sv_max = __uint_as_float(vbits);
+
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true;
+  for (int j = 0; j < n_steps; ++j) {
+    int c, tt, valid;
+    bool extra;
+    step_info(p, j, c, tt, valid, extra);
+    float sk, sv;
+    if (extra) {
+      const int idx = bh * p.kvx_bh + q_tile_c * p.kvx_blk;
+      sk = p.ksx[idx];
+      sv = p.vsx[idx];
+    } else {
+      const int64_t idx = c * p.kv_chunk + bh * p.kv_bh + tt * p.kv_blk;
+      sk = p.ks[idx];
+      sv = p.vs[idx];
+    }
+    const float cj = p.sm_scale_log2 * sq * sk;
+    const float kj = 448.f * (sv / sv_max);
+    const float log2k = __log2f(kj);
+
+    if (!warp_wait(bar.s_full + t, j & 1, bar.abort_flag, p.status, kErrWaitS)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    uint32_t r[4][32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, r[q]);
+    tmem_wait_ld();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar.s_free + t);
+
+    float s[128];
+#pragma unroll
+    for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(r[i >> 5][i & 31]);
+
+    if (!extra && valid < kTile) {
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (i >= valid) s[i] = -INFINITY;
+    }
+    if (p.causal) {
+      const int rel = (q_tile * kTile + row) - tt * kTile;  // column i allowed iff i <= rel
+      if (rel < kTile - 1) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i > rel) s[i] = -INFINITY;
+      }
+    }
+    if (extra) {
+      const int g0 = (row / p.extra_group) * p.extra_group;  // own candidate's first token
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (i < g0 || i > row) s[i] = -INFINITY;
+    }
+
+    float mx = s[0];
+#pragma unroll
+    for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+    const float m_new = fmaxf(m_run, mx * cj);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float alpha = ex2_approx(m_run - m_use);
+    const float noff = log2k - m_use;
+
+    uint32_t pk[32];
+    uint32_t pl[(PMODE == 1) ? 32 : 1];
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float e0 = ex2_approx(fmaf(s[4 * i + 0], cj, noff));
+      const float e1 = ex2_approx(fmaf(s[4 * i + 1], cj, noff));
+      const float e2 = ex2_approx(fmaf(s[4 * i + 2], cj, noff));
+      const float e3 = ex2_approx(fmaf(s[4 * i + 3], cj, noff));
+      sum += (e0 + e1) + (e2 + e3);
+      pk[i] = pack_e4m3x4(e0, e1, e2, e3);
+      if constexpr (PMODE == 1) pl[i] = pack_e4m3x4_residual(pk[i], e0, e1, e2, e3);
+    }
+
+    if (C::kPBuf == 1 && j > 0) {
+      if (!warp_wait(bar.o_done + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
+        ok = false;
+        break;
+      }
+    }
+    uint8_t* pb = pbase + ((C::kPBuf == 2) ? (j & 1) : 0) * C::kPStride;
+    const uint32_t prow = smem_u32(pb) + row * 128;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      st_shared_v4(prow + ((k ^ (row & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
+                   pk[4 * k + 3]);
+    if constexpr (PMODE == 1) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        st_shared_v4(prow + kTileBytes + ((k ^ (row & 7)) << 4), pl[4 * k], pl[4 * k + 1],
+                     pl[4 * k + 2], pl[4 * k + 3]);
+    }
+    fence_proxy_async_smem();
+
+    if (j > 0) {
+      if (C::kPBuf == 2 &&
+          !warp_wait(bar.o_done + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * q, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + 32 * q, o);
+        }
+        tmem_wait_st();
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar.p_full + t);
+    l_run = l_run * alpha + sum / kj;
+    m_run = m_new;
+  }
+
+  if (ok && n_steps > 0)
+    ok = warp_wait(bar.o_done + t, (n_steps - 1) & 1, bar.abort_flag, p.status, kErrWaitO);
+  if (!ok) return;
+
+  // Epilogue: O * (sv_max / 448) / l -> bf16, staged as two 128x64 halves in
+  // this tile's (now idle) Q and P buffers, written by TMA.
+  tc_fence_after();
+  const float f = (sv_max / 448.f) / l_run;
+  uint8_t* stage[2] = {smem + C::kOffQ + t * kTileBytes, pbase};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t srow = smem_u32(stage[h]) + row * 128;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      uint32_t o[32];
+      tmem_ld32(tO + 64 * h + 32 * cc, o);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int k = cc * 4 + q;
+        const float* v = reinterpret_cast<const float*>(o) + 8 * q;
+        st_shared_v4(srow + ((k ^ (row & 7)) << 4), pack_bf16x2(v[0] * f, v[1] * f),
+                     pack_bf16x2(v[2] * f, v[3] * f), pack_bf16x2(v[4] * f, v[5] * f),
+                     pack_bf16x2(v[6] * f, v[7] * f));
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar.epi + t);
+  if (wq == 0 && lane == 0 && q_tile < p.n_q_tiles) {
+    if (mbar_wait(bar.epi + t, 0, bar.abort_flag, p.status, kErrWaitEpi)) {
+      const int b = bh / p.H, h = bh % p.H;
+      tma_store_4d(tm_o, stage[0], 0, q_tile * kTile, h, b);
+      tma_store_4d(tm_o, stage[1], 64, q_tile * kTile, h, b);
+      tma_store_commit();
+      tma_store_wait0();
+    }
+  }
+}
+
+template <int NQ, int PMODE>
+__global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
+    fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v,
+                   const __grid_constant__ CUtensorMap tm_kx,
+                   const __grid_constant__ CUtensorMap tm_vx,
+                   const __grid_constant__ CUtensorMap tm_o, const AttnKernelParams p) {
+  using C = Cfg<NQ, PMODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const Bars bar = carve_bars<NQ>(smem + C::kOffBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar.q_full, 1);
+    for (int i = 0; i < kKSt; ++i) {
+      mbar_init(bar.k_full + i, 1);
+      mbar_init(bar.k_empty + i, 1);
+    }
+    for (int i = 0; i < kVSt; ++i) {
+      mbar_init(bar.v_full + i, 1);
+      mbar_init(bar.v_empty + i, 1);
+    }
+    for (int t = 0; t < NQ; ++t) {
+      mbar_init(bar.s_full + t, 1);
+      mbar_init(bar.s_free + t, 4);
+      mbar_init(bar.p_full + t, 4);
+      mbar_init(bar.o_done + t, 1);
+      mbar_init(bar.epi + t, 4);
+    }
+    mbar_init(bar.fin, 1);
+    *bar.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == C::kMmaWarp) {
+    tmem_alloc(bar.tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == C::kTmaWarp && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *bar.tmem_slot;
+
+  int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
+  if (p.causal) {
+    const int last_row = min(p.Sq, (blockIdx.x * NQ + NQ) * kTile) - 1;
+    n_steps = min(n_steps, last_row / kTile + 1);
+  }
+
+  if (warp == C::kTmaWarp) {
+    if (lane == 0) producer<NQ, PMODE>(&tm_q, &tm_k, &tm_v, &tm_kx, &tm_vx, p, bar, smem, n_steps);
+  } else if (warp == C::kMmaWarp) {
+    if (lane == 0) mma_issuer<NQ, PMODE>(p, bar, smem, tmem, n_steps);
+  } else {
+    softmax_wg<NQ, PMODE>(&tm_o, p, bar, smem, tmem, n_steps);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == C::kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+template <int NQ, int PMODE>
+cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
+                           cudaStream_t st) {
+  using C = Cfg<NQ, PMODE>;
+  auto kern = fa8_fwd_kernel<NQ, PMODE>;
+  // Opt in to the large dynamic shared-memory carve-out once per device.
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit, std::memory_order_release);
+  }
+  const dim3 grid((p.n_q_tiles + NQ - 1) / NQ, B * H);
+  kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(m.q, m.k, m.v, m.kx, m.vx, m.o, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
+                             int nq, int p_mode, cudaStream_t st) {
+  if (nq == 2 && p_mode == 0) return launch_variant<2, 0>(maps, p, B, H, st);
+  if (nq == 2 && p_mode == 1) return launch_variant<2, 1>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 0) return launch_variant<1, 0>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 1) return launch_variant<1, 1>(maps, p, B, H, st);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace rp

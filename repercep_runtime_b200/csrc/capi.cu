@@ -1,0 +1,402 @@
+// extern "C" entry points of librepercep_b200.so (declared in
+// include/repercep_b200.h): argument checking, TMA descriptor encoding and
+// kernel launch.  No exception crosses the boundary; failures return a
+// negative rp_status and leave a message for rp_last_error().
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/repercep_b200.h"
+#include "internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(RP_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Device status word: kernels whose pipeline wait timed out record a code.
+__device__ int g_rp_status;
+
+struct DeviceState {
+  bool probed = false;
+  bool sm100 = false;
+  int* status = nullptr;
+};
+std::mutex g_mu;
+DeviceState g_dev[64];
+
+// Checks that the current device is sm_100 and returns its status word.
+int device_ready(int** status) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(RP_ERR_INVALID, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (!d.probed) {
+    int major = 0, minor = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    d.sm100 = (major == 10 && minor == 0);
+    if (d.sm100) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_rp_status);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+      d.status = static_cast<int*>(p);
+    }
+    d.probed = true;
+  }
+  if (!d.sm100) return fail(RP_ERR_ARCH, "device %d is not sm_100 (B200); this library is sm_100a only", dev);
+  *status = d.status;
+  return RP_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                        &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Rank-4 tiled map.  strides[] are byte strides of dims 1..3.  A dimension
+// of extent 1 gets a harmless stride so the encoder's checks pass.
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, const uint64_t dims[4],
+             uint64_t strides[3], const uint32_t box[4], const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(RP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return fail(RP_ERR_ALIGN, "%s: base address must be 16-byte aligned", what);
+  for (int i = 0; i < 3; ++i) {
+    if (dims[i + 1] == 1) strides[i] = (i == 0) ? 16 * ((dims[0] * 2 + 15) / 16) : strides[i - 1];
+    if (strides[i] % 16 != 0)
+      return fail(RP_ERR_ALIGN, "%s: byte stride %llu of dim %d is not a multiple of 16", what,
+                  (unsigned long long)strides[i], i + 1);
+  }
+  const uint32_t elem_strides[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, elem_strides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(RP_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return RP_OK;
+}
+
+// e4m3 operand stored (chunks, rows_per_chunk, bh, 128): one 128x128 box.
+int make_fp8_map(CUtensorMap* m, const void* base, int rows, int bh, int chunks, const char* what) {
+  const uint64_t dims[4] = {128, (uint64_t)rows, (uint64_t)bh, (uint64_t)chunks};
+  uint64_t strides[3] = {128, (uint64_t)rows * 128, (uint64_t)rows * 128 * bh};
+  const uint32_t box[4] = {128, 128, 1, 1};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, dims, strides, box, what);
+}
+
+// bf16 output (B, H, S, 128) with element strides {sB, sH, sS}: stored as
+// two 64-column boxes per 128-row tile.
+int make_out_map(CUtensorMap* m, void* base, int B, int H, int S, int64_t sB, int64_t sH,
+                 int64_t sS) {
+  const uint64_t dims[4] = {128, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+  uint64_t strides[3] = {(uint64_t)sS * 2, (uint64_t)sH * 2, (uint64_t)sB * 2};
+  const uint32_t box[4] = {64, 128, 1, 1};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, dims, strides, box, "out");
+}
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+}  // namespace
+
+extern "C" {
+
+int rp_abi_version(void) { return RP_ABI_VERSION; }
+
+const char* rp_last_error(void) { return g_last_error.c_str(); }
+
+int rp_device_status(int* status, int reset) {
+  if (!status) return fail(RP_ERR_INVALID, "status is null");
+  int* dummy = nullptr;
+  int rc = device_ready(&dummy);
+  if (rc != RP_OK) return rc;
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_rp_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_rp_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "reset status");
+  }
+  return RP_OK;
+}
+
+int rp_quant_workspace_bytes(int num_tensors, int B, int H, int S, int D, int scale_mode,
+                             size_t* bytes) {
+  if (!bytes) return fail(RP_ERR_INVALID, "bytes is null");
+  if (num_tensors < 1 || num_tensors > rp::kMaxQuantJobs || B <= 0 || H <= 0 || S <= 0 || D <= 0)
+    return fail(RP_ERR_INVALID, "bad quantize shape");
+  if (scale_mode == RP_SCALE_PER_BLOCK128) {
+    *bytes = 0;
+  } else if (scale_mode == RP_SCALE_PER_BH) {
+    *bytes = (size_t)num_tensors * B * H * ceil_div(S, rp::kQuantRows) * sizeof(uint32_t);
+  } else {
+    return fail(RP_ERR_INVALID, "unknown scale_mode %d", scale_mode);
+  }
+  return RP_OK;
+}
+
+int rp_quant_fp8_e4m3(int num_tensors, const void* const* x, const int64_t* strides, int B, int H,
+                      int S, int D, int scale_mode, void* const* out, float* const* scales,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_tensors < 1 || num_tensors > rp::kMaxQuantJobs)
+    return fail(RP_ERR_INVALID, "num_tensors must be 1..3 (got %d)", num_tensors);
+  if (!x || !strides || !out || !scales) return fail(RP_ERR_INVALID, "null argument array");
+  if (B <= 0 || H <= 0 || S <= 0) return fail(RP_ERR_INVALID, "B, H, S must be positive");
+  if (D != 32 && D != 64 && D != 128 && D != 256)
+    return fail(RP_ERR_UNSUPPORTED, "head_dim %d not in {32,64,128,256}", D);
+  if ((int64_t)B * H > 65535) return fail(RP_ERR_UNSUPPORTED, "B*H > 65535");
+  size_t need = 0;
+  int rc = rp_quant_workspace_bytes(num_tensors, B, H, S, D, scale_mode, &need);
+  if (rc != RP_OK) return rc;
+  if (need > 0 && (!workspace || workspace_bytes < need))
+    return fail(RP_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+  int* status = nullptr;
+  rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+
+  rp::QuantArgs a{};
+  a.B = B;
+  a.H = H;
+  a.S = S;
+  a.D = D;
+  a.nblk = ceil_div(S, rp::kQuantRows);
+  a.partial = static_cast<uint32_t*>(workspace);
+  for (int i = 0; i < num_tensors; ++i) {
+    const int64_t* st = strides + 4 * i;
+    if (!x[i] || !out[i] || !scales[i]) return fail(RP_ERR_INVALID, "tensor %d: null pointer", i);
+    if (st[3] != 1) return fail(RP_ERR_UNSUPPORTED, "tensor %d: head dim must be unit-stride", i);
+    if (!aligned16(x[i]) || (st[0] % 8) || (st[1] % 8) || (st[2] % 8))
+      return fail(RP_ERR_ALIGN, "tensor %d: base and strides must be 16-byte multiples", i);
+    if (!aligned16(out[i])) return fail(RP_ERR_ALIGN, "tensor %d: output must be 16-byte aligned", i);
+    a.job[i].x = static_cast<const uint16_t*>(x[i]);
+    a.job[i].sB = st[0];
+    a.job[i].sH = st[1];
+    a.job[i].sS = st[2];
+    a.job[i].out = static_cast<uint8_t*>(out[i]);
+    a.job[i].scales = scales[i];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = (scale_mode == RP_SCALE_PER_BLOCK128) ? rp::launch_quant_block(a, num_tensors, s)
+                                                        : rp::launch_quant_bh(a, num_tensors, s);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  return RP_OK;
+}
+
+namespace {
+
+int check_attn_common(const void* q8, const void* k8, const void* v8, const float* qs,
+                      const float* ks, const float* vs, int D, int p_mode, void* out,
+                      const int64_t* out_strides, int n_out_strides) {
+  if (!q8 || !k8 || !v8 || !qs || !ks || !vs || !out || !out_strides)
+    return fail(RP_ERR_INVALID, "null pointer argument");
+  if (D != 128) return fail(RP_ERR_UNSUPPORTED, "head_dim %d: this kernel is built for 128", D);
+  if (p_mode != RP_P_E4M3 && p_mode != RP_P_E4M3_HILO)
+    return fail(RP_ERR_INVALID, "unknown p_mode %d", p_mode);
+  if (out_strides[n_out_strides - 1] != 1)
+    return fail(RP_ERR_UNSUPPORTED, "output head dim must be unit-stride");
+  if (!aligned16(q8) || !aligned16(k8) || !aligned16(v8) || !aligned16(out))
+    return fail(RP_ERR_ALIGN, "tensors must be 16-byte aligned");
+  return RP_OK;
+}
+
+rp::AttnKernelParams base_params(int H, int Sq, float sm_scale, int D, int* status) {
+  rp::AttnKernelParams p{};
+  p.H = H;
+  p.Sq = Sq;
+  p.n_q_tiles = ceil_div(Sq, 128);
+  p.has_extra = 0;
+  p.extra_group = 1;
+  const float scale = (sm_scale > 0.f) ? sm_scale : 1.0f / std::sqrt(static_cast<float>(D));
+  p.sm_scale_log2 = scale * kLog2e;
+  p.status = status;
+  return p;
+}
+
+}  // namespace
+
+int rp_attn_fp8_fwd(const void* q8, const void* k8, const void* v8, const float* qs,
+                    const float* ks, const float* vs, int scale_mode, int B, int H, int Sq,
+                    int Skv, int D, float sm_scale, int causal, int p_mode, void* out,
+                    const int64_t* out_strides, void* stream) {
+  int rc = check_attn_common(q8, k8, v8, qs, ks, vs, D, p_mode, out, out_strides, 4);
+  if (rc != RP_OK) return rc;
+  if (B <= 0 || H <= 0 || Sq <= 0 || Skv <= 0)
+    return fail(RP_ERR_INVALID, "B, H, Sq, Skv must be positive");
+  if ((int64_t)B * H > 65535) return fail(RP_ERR_UNSUPPORTED, "B*H > 65535");
+  if (scale_mode != RP_SCALE_PER_BH && scale_mode != RP_SCALE_PER_BLOCK128)
+    return fail(RP_ERR_INVALID, "unknown scale_mode %d", scale_mode);
+  int* status = nullptr;
+  rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+
+  const int BH = B * H;
+  rp::AttnMaps m;
+  if ((rc = make_fp8_map(&m.q, q8, Sq, BH, 1, "q")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.k, k8, Skv, BH, 1, "k")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.v, v8, Skv, BH, 1, "v")) != RP_OK) return rc;
+  m.kx = m.k;
+  m.vx = m.v;
+  if ((rc = make_out_map(&m.o, out, B, H, Sq, out_strides[0], out_strides[1], out_strides[2])) != RP_OK)
+    return rc;
+
+  rp::AttnKernelParams p = base_params(H, Sq, sm_scale, D, status);
+  const int nq_blk = ceil_div(Sq, 128), nk_blk = ceil_div(Skv, 128);
+  p.n_chunks = 1;
+  p.tiles_per_chunk = nk_blk;
+  p.chunk_len = Skv;
+  p.last_len = Skv;
+  p.n_main_tiles = nk_blk;
+  const bool per_bh = (scale_mode == RP_SCALE_PER_BH);
+  p.qs = qs;
+  p.qs_bh = per_bh ? 1 : nq_blk;
+  p.qs_blk = per_bh ? 0 : 1;
+  p.ks = ks;
+  p.vs = vs;
+  p.kv_chunk = 0;
+  p.kv_bh = per_bh ? 1 : nk_blk;
+  p.kv_blk = per_bh ? 0 : 1;
+  p.ksx = ks;
+  p.vsx = vs;
+  p.causal = causal ? 1 : 0;
+  cudaError_t e = rp::launch_attention(m, p, B, H, 2, p_mode, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return RP_OK;
+}
+
+int rp_attn_fp8_fwd_chunked(const void* q8, const void* k8, const void* v8, const float* qs,
+                            const float* ks, const float* vs, int B, int H, int Sq,
+                            int n_chunks, int chunk_rows, int last_rows, int D, float sm_scale,
+                            int p_mode, void* out, const int64_t* out_strides, void* stream) {
+  int rc = check_attn_common(q8, k8, v8, qs, ks, vs, D, p_mode, out, out_strides, 4);
+  if (rc != RP_OK) return rc;
+  if (B <= 0 || H <= 0 || Sq <= 0 || n_chunks <= 0 || chunk_rows <= 0 || last_rows <= 0 ||
+      last_rows > chunk_rows)
+    return fail(RP_ERR_INVALID, "bad chunked shape");
+  if (n_chunks > 1 && chunk_rows % 128 != 0)
+    return fail(RP_ERR_UNSUPPORTED, "chunk_rows must be a multiple of 128 when n_chunks > 1");
+  if ((int64_t)B * H > 65535 || n_chunks > 65535) return fail(RP_ERR_UNSUPPORTED, "grid too large");
+  int* status = nullptr;
+  rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+
+  const int BH = B * H;
+  rp::AttnMaps m;
+  if ((rc = make_fp8_map(&m.q, q8, Sq, BH, 1, "q")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.k, k8, chunk_rows, BH, n_chunks, "k")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.v, v8, chunk_rows, BH, n_chunks, "v")) != RP_OK) return rc;
+  m.kx = m.k;
+  m.vx = m.v;
+  if ((rc = make_out_map(&m.o, out, B, H, Sq, out_strides[0], out_strides[1], out_strides[2])) != RP_OK)
+    return rc;
+
+  rp::AttnKernelParams p = base_params(H, Sq, sm_scale, D, status);
+  const int nblk_c = ceil_div(chunk_rows, 128);
+  p.n_chunks = n_chunks;
+  p.tiles_per_chunk = nblk_c;
+  p.chunk_len = chunk_rows;
+  p.last_len = last_rows;
+  p.n_main_tiles = (n_chunks - 1) * nblk_c + ceil_div(last_rows, 128);
+  p.qs = qs;
+  p.qs_bh = ceil_div(Sq, 128);
+  p.qs_blk = 1;
+  p.ks = ks;
+  p.vs = vs;
+  p.kv_chunk = (int64_t)BH * nblk_c;
+  p.kv_bh = nblk_c;
+  p.kv_blk = 1;
+  p.ksx = ks;
+  p.vsx = vs;
+  p.causal = 0;
+  cudaError_t e = rp::launch_attention(m, p, B, H, 2, p_mode, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return RP_OK;
+}
+
+int rp_attn_fp8_prefix_decode(const void* q8, const void* kp8, const void* vp8,
+                              const void* kx8, const void* vx8, const float* qs,
+                              const float* kps, const float* vps, const float* kxs,
+                              const float* vxs, int C, int T, int P, int H, int D,
+                              float sm_scale, int p_mode, void* out,
+                              const int64_t* out_strides, void* stream) {
+  int rc = check_attn_common(q8, kp8, vp8, qs, kps, vps, D, p_mode, out, out_strides, 3);
+  if (rc != RP_OK) return rc;
+  if (!kx8 || !vx8 || !kxs || !vxs) return fail(RP_ERR_INVALID, "null suffix argument");
+  if (!aligned16(kx8) || !aligned16(vx8)) return fail(RP_ERR_ALIGN, "suffix must be 16-byte aligned");
+  if (C <= 0 || T <= 0 || P <= 0 || H <= 0) return fail(RP_ERR_INVALID, "C, T, P, H must be positive");
+  if (128 % T != 0) return fail(RP_ERR_UNSUPPORTED, "tokens per candidate (%d) must divide 128", T);
+  if (H > 65535) return fail(RP_ERR_UNSUPPORTED, "H > 65535");
+  int* status = nullptr;
+  rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+
+  const int rows = C * T;
+  rp::AttnMaps m;
+  if ((rc = make_fp8_map(&m.q, q8, rows, H, 1, "q")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.k, kp8, P, H, 1, "k_prefix")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.v, vp8, P, H, 1, "v_prefix")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.kx, kx8, rows, H, 1, "k_suffix")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.vx, vx8, rows, H, 1, "v_suffix")) != RP_OK) return rc;
+  if ((rc = make_out_map(&m.o, out, 1, H, rows, 0, out_strides[1], out_strides[0])) != RP_OK)
+    return rc;
+
+  rp::AttnKernelParams p = base_params(H, rows, sm_scale, D, status);
+  const int nq_blk = ceil_div(rows, 128), np_blk = ceil_div(P, 128);
+  p.n_chunks = 1;
+  p.tiles_per_chunk = np_blk;
+  p.chunk_len = P;
+  p.last_len = P;
+  p.n_main_tiles = np_blk;
+  p.has_extra = 1;
+  p.extra_group = T;
+  p.qs = qs;
+  p.qs_bh = nq_blk;
+  p.qs_blk = 1;
+  p.ks = kps;
+  p.vs = vps;
+  p.kv_chunk = 0;
+  p.kv_bh = np_blk;
+  p.kv_blk = 1;
+  p.ksx = kxs;
+  p.vsx = vxs;
+  p.kvx_bh = nq_blk;
+  p.kvx_blk = 1;
+  p.causal = 0;
+  cudaError_t e = rp::launch_attention(m, p, 1, H, 1, p_mode, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return RP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,66 @@
+// Host/device declarations shared by the .cu files of librepercep_b200.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace rp {
+
+// ------------------------------------------------------------- quantize
+constexpr int kQuantRows = 128;     // tokens per scale block / per CTA
+constexpr int kQuantThreads = 256;  // threads per quantize CTA
+constexpr int kMaxQuantJobs = 3;    // Q, K, V in one launch
+
+struct QuantJob {
+  const uint16_t* x;   // bf16 input, element (b,h,s,d) at b*sB + h*sH + s*sS + d
+  int64_t sB, sH, sS;  // element strides (d is unit-stride)
+  uint8_t* out;        // e4m3, contiguous (B*H, S, D)
+  float* scales;       // (B*H,) per-(b,h) or (B*H, nblk) per block
+};
+
+struct QuantArgs {
+  QuantJob job[kMaxQuantJobs];
+  int B, H, S, D;
+  int nblk;            // ceil(S / 128)
+  uint32_t* partial;   // per-(b,h) mode: (njobs, B*H, nblk) partial amax bits
+};
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_quant_block(const QuantArgs& a, int njobs, cudaStream_t st);
+cudaError_t launch_quant_bh(const QuantArgs& a, int njobs, cudaStream_t st);
+
+// ------------------------------------------------------------ attention
+struct AttnKernelParams {
+  int H;                 // heads (bh -> (b, h) for the output map)
+  int Sq;                // query rows per (b,h)
+  int n_q_tiles;         // ceil(Sq / 128)
+  // Main K/V source: n_chunks chunks; all but the last hold chunk_len rows
+  // (a multiple of 128), the last holds last_len rows.
+  int n_chunks, tiles_per_chunk, chunk_len, last_len, n_main_tiles;
+  // Extra K/V tile per query tile (shared-prefix decode suffix).
+  int has_extra, extra_group;
+  // Scales (dequant multipliers).
+  const float* qs;
+  int qs_bh, qs_blk;
+  const float* ks;
+  const float* vs;
+  int64_t kv_chunk;      // scale index = c*kv_chunk + bh*kv_bh + t*kv_blk
+  int kv_bh, kv_blk;
+  const float* ksx;
+  const float* vsx;
+  int kvx_bh, kvx_blk;   // extra scale index = bh*kvx_bh + qtile*kvx_blk
+  float sm_scale_log2;   // softmax scale * log2(e)
+  int causal;
+  int* status;           // device status word (0 = ok)
+};
+
+struct AttnMaps {
+  CUtensorMap q, k, v, kx, vx, o;
+};
+
+cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
+                             int nq, int p_mode, cudaStream_t st);
+
+}  // namespace rp

@@ -1,0 +1,206 @@
+// bf16 -> e4m3 quantization with amax scales.
+//
+// Semantics (bit-exact with the reference's eager PyTorch quantizer,
+// kernels/triton_kernels/fp8_flash_attn_hopper.py:374-398):
+//   amax   = max |x| over the scale group, taken in bf16 (NaN propagates)
+//   amax   = max(amax, bf16(1e-6))                         (clamp in bf16)
+//   scale  = bf16_rne(float(amax) / 425.6f)   -> dequant scale, stored f32
+//   q_mul  = 1 / scale                          (IEEE round-to-nearest)
+//   y      = clamp(float(x) * q_mul, -448, 448)
+//   byte   = e4m3fn_rne(y)                      (NaN -> 0x7F | sign)
+// 425.6f is float(0.95 * 448).  For every bf16 amax, the fp32 quotient and
+// the fp32 product with the rounded reciprocal (PyTorch's CUDA path) round
+// to the same bf16, so one formula covers both of the reference's devices.
+//
+// Scale groups: one per (b,h) (the reference) or one per 128-token block of
+// each (b,h) (the per-block extension; the last block of a ragged S is short).
+//
+// The input is read through arbitrary (b,h,s) element strides with d
+// unit-stride, so BHSD and BSHD (diffusers) tensors need no transposing copy.
+// Output is always contiguous (B*H, S, D).
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "internal.h"
+
+namespace rp {
+
+namespace {
+
+constexpr uint32_t kAmaxFloorBits = 0x3586u;  // bf16 nearest to 1e-6
+constexpr float kScaleDiv = 425.6f;           // float(0.95 * 448)
+
+__device__ __forceinline__ float scale_from_amax_bits(uint32_t amax_bits) {
+  uint32_t b = amax_bits;
+  // Clamp to the floor; NaN (bits > 0x7F80) is kept, like torch.clamp.
+  if (b <= 0x7F80u && b < kAmaxFloorBits) b = kAmaxFloorBits;
+  const float a = __uint_as_float(b << 16);
+  const float s = __fdiv_rn(a, kScaleDiv);
+  return __bfloat162float(__float2bfloat16_rn(s));
+}
+
+__device__ __forceinline__ uint32_t quant_byte(float x, float qm) {
+  float y = __fmul_rn(x, qm);
+  y = (y > 448.f) ? 448.f : y;   // comparisons keep NaN
+  y = (y < -448.f) ? -448.f : y;
+  if (y != y) return 0x7Fu | ((__float_as_uint(y) >> 24) & 0x80u);
+  return static_cast<uint32_t>(__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3));
+}
+
+// 8 bf16 (one 16-byte vector) -> 8 e4m3 bytes.
+__device__ __forceinline__ uint2 quant8(uint4 v, float qm) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t a = w[2 * i], b = w[2 * i + 1];
+    const uint32_t b0 = quant_byte(__uint_as_float(a << 16), qm);
+    const uint32_t b1 = quant_byte(__uint_as_float(a & 0xFFFF0000u), qm);
+    const uint32_t b2 = quant_byte(__uint_as_float(b << 16), qm);
+    const uint32_t b3 = quant_byte(__uint_as_float(b & 0xFFFF0000u), qm);
+    o[i] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+  }
+  return make_uint2(o[0], o[1]);
+}
+
+// max of |bf16| bit patterns held in a 16-byte vector.
+__device__ __forceinline__ uint32_t absmax8(uint4 v) {
+  uint32_t m = __vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu);
+  m = __vmaxu2(m, v.z & 0x7FFF7FFFu);
+  m = __vmaxu2(m, v.w & 0x7FFF7FFFu);
+  return max(m & 0xFFFFu, m >> 16);
+}
+
+__device__ __forceinline__ uint32_t block_max(uint32_t v, uint32_t* red) {
+  v = __reduce_max_sync(0xffffffffu, v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < kQuantThreads / 32; ++i) m = max(m, red[i]);
+  return m;
+}
+
+// One CTA = one 128-token block of one (b,h) of one job.  D/8 vectors per
+// row, 128 rows: each thread holds D/16 vectors in registers.
+template <int D>
+struct BlockTile {
+  static constexpr int kVpr = D / 8;
+  static constexpr int kPer = kQuantRows * kVpr / kQuantThreads;
+  uint4 v[kPer];
+
+  __device__ __forceinline__ uint32_t load(const QuantJob& j, int b, int h, int s0, int rows) {
+    const uint16_t* base = j.x + b * j.sB + h * j.sH;
+    uint32_t m = 0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int idx = threadIdx.x + k * kQuantThreads;
+      const int r = idx / kVpr, c = idx % kVpr;
+      if (r < rows) {
+        v[k] = __ldcs(reinterpret_cast<const uint4*>(base + (int64_t)(s0 + r) * j.sS + c * 8));
+        m = max(m, absmax8(v[k]));
+      } else {
+        v[k] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    return m;
+  }
+
+  __device__ __forceinline__ void store(const QuantJob& j, int bh, int S, int s0, int rows,
+                                        float qm) {
+    uint8_t* out = j.out + ((int64_t)bh * S + s0) * D;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int idx = threadIdx.x + k * kQuantThreads;
+      const int r = idx / kVpr, c = idx % kVpr;
+      if (r < rows) __stcs(reinterpret_cast<uint2*>(out + (int64_t)r * D + c * 8), quant8(v[k], qm));
+    }
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(kQuantThreads) quant_block_kernel(const QuantArgs a) {
+  __shared__ uint32_t red[kQuantThreads / 32];
+  const QuantJob& j = a.job[blockIdx.z];
+  const int blk = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / a.H, h = bh % a.H;
+  const int s0 = blk * kQuantRows;
+  const int rows = min(kQuantRows, a.S - s0);
+  BlockTile<D> t;
+  const uint32_t m = block_max(t.load(j, b, h, s0, rows), red);
+  const float sc = scale_from_amax_bits(m);
+  if (threadIdx.x == 0) j.scales[(int64_t)bh * a.nblk + blk] = sc;
+  t.store(j, bh, a.S, s0, rows, __frcp_rn(sc));
+}
+
+// Per-(b,h) pass 1: partial amax of one 128-row chunk.
+template <int D>
+__global__ void __launch_bounds__(kQuantThreads) amax_chunk_kernel(const QuantArgs a) {
+  __shared__ uint32_t red[kQuantThreads / 32];
+  const QuantJob& j = a.job[blockIdx.z];
+  const int blk = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / a.H, h = bh % a.H;
+  const int s0 = blk * kQuantRows;
+  const int rows = min(kQuantRows, a.S - s0);
+  const uint16_t* base = j.x + b * j.sB + h * j.sH;
+  constexpr int kVpr = D / 8;
+  uint32_t m = 0;
+  for (int idx = threadIdx.x; idx < rows * kVpr; idx += kQuantThreads) {
+    const int r = idx / kVpr, c = idx % kVpr;
+    m = max(m, absmax8(__ldg(reinterpret_cast<const uint4*>(base + (int64_t)(s0 + r) * j.sS + c * 8))));
+  }
+  m = block_max(m, red);
+  if (threadIdx.x == 0)
+    a.partial[((int64_t)blockIdx.z * gridDim.y + bh) * a.nblk + blk] = m;
+}
+
+// Per-(b,h) pass 2: reduce the partials of this (b,h), quantize one chunk.
+template <int D>
+__global__ void __launch_bounds__(kQuantThreads) quant_bh_kernel(const QuantArgs a) {
+  __shared__ uint32_t red[kQuantThreads / 32];
+  const QuantJob& j = a.job[blockIdx.z];
+  const int blk = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / a.H, h = bh % a.H;
+  const uint32_t* part = a.partial + ((int64_t)blockIdx.z * gridDim.y + bh) * a.nblk;
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < a.nblk; i += kQuantThreads) m = max(m, part[i]);
+  m = block_max(m, red);
+  const float sc = scale_from_amax_bits(m);
+  if (blk == 0 && threadIdx.x == 0) j.scales[bh] = sc;
+  const int s0 = blk * kQuantRows;
+  const int rows = min(kQuantRows, a.S - s0);
+  BlockTile<D> t;
+  t.load(j, b, h, s0, rows);
+  t.store(j, bh, a.S, s0, rows, __frcp_rn(sc));
+}
+
+}  // namespace
+
+#define RP_DISPATCH_D(KERNEL)                                                        \
+  switch (a.D) {                                                                     \
+    case 32: KERNEL<32><<<grid, kQuantThreads, 0, st>>>(a); break;                  \
+    case 64: KERNEL<64><<<grid, kQuantThreads, 0, st>>>(a); break;                  \
+    case 128: KERNEL<128><<<grid, kQuantThreads, 0, st>>>(a); break;                \
+    case 256: KERNEL<256><<<grid, kQuantThreads, 0, st>>>(a); break;                \
+    default: return cudaErrorInvalidValue;                                           \
+  }
+
+cudaError_t launch_quant_block(const QuantArgs& a, int njobs, cudaStream_t st) {
+  const dim3 grid(a.nblk, a.B * a.H, njobs);
+  RP_DISPATCH_D(quant_block_kernel)
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_bh(const QuantArgs& a, int njobs, cudaStream_t st) {
+  const dim3 grid(a.nblk, a.B * a.H, njobs);
+  RP_DISPATCH_D(amax_chunk_kernel)
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  RP_DISPATCH_D(quant_bh_kernel)
+  return cudaGetLastError();
+}
+
+#undef RP_DISPATCH_D
+
+}  // namespace rp
