@@ -78,7 +78,9 @@ def test_attention_small(case, mode, p_mode):
     k8, ks = _quant_np(k, mode)
     v8, vs = _quant_np(v, mode)
     ref = oa.attention_dequant(q8, k8, v8, qs, ks, vs, 1 / math.sqrt(128), causal=causal)
-    _check(out.reshape(B * H, Sq, 128), ref)
+    # Causal rows near the diagonal average only a few keys, so the reference-
+    # precision P (p_mode 0) error is not averaged out there: relative bound.
+    _check(out.reshape(B * H, Sq, 128), ref, relative=causal and p_mode == 0)
 
 
 def test_attention_matches_reference_tile_loop():
