@@ -28,6 +28,7 @@
 #include <cuda_fp8.h>
 
 #include <atomic>
+#include <cstdlib>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -39,6 +40,26 @@ constexpr int kTile = 128;
 constexpr int kTileBytes = kTile * kTile;
 constexpr int kKSt = 3;
 constexpr int kVSt = 3;
+constexpr int kDefaultExpPoly = 0;
+
+// Pipeline tracing (compiled in only with -DRP_PIPELINE_TRACE): one chosen CTA
+// records (SM clock, event << 16 | step) at every barrier hand-off of every
+// role, for offline timeline analysis.  The product build has none of it.
+#ifdef RP_PIPELINE_TRACE
+// Slot (event, step) of the traced CTA; plain stores, so recording does not
+// stall the recording thread.
+__device__ uint32_t* g_trace_buf;
+__device__ int g_trace_x;
+__device__ int g_trace_y;
+constexpr int kTraceSteps = 1024;
+__device__ __forceinline__ void trace_event(int ev, int j) {
+  if ((int)blockIdx.x != g_trace_x || (int)blockIdx.y != g_trace_y) return;
+  g_trace_buf[ev * kTraceSteps + (j & (kTraceSteps - 1))] = static_cast<uint32_t>(clock64());
+}
+#define RP_TRACE(ev, j) trace_event((ev), (j))
+#else
+#define RP_TRACE(ev, j) ((void)0)
+#endif
 
 enum : int {
   kErrWaitQ = 0x101,
@@ -150,6 +171,27 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// 2^x for two lanes on the FMA pipe: x = n + f with n = rint(x) (the 1.5*2^23
+// addition rounds into the low mantissa bits), 2^f from a cubic fitted on
+// [-0.5, 0.5] (csrc/gen_exp2_poly.py, max relative error 7.5e-5), 2^n added to
+// the exponent field as an integer.  Inputs are clamped to >= -125 so the
+// exponent never wraps; results below 2^-125 are irrelevant to the softmax.
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t x = pack_f32x2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = fadd2(x, pack_f32x2(kRound, kRound));
+  const uint64_t f = fsub2(x, fsub2(t, pack_f32x2(kRound, kRound)));
+  uint64_t q = ffma2(pack_f32x2(0.055170513689517975f, 0.055170513689517975f), f,
+                     pack_f32x2(0.24260854721069336f, 0.24260854721069336f));
+  q = ffma2(q, f, pack_f32x2(0.6932609677314758f, 0.6932609677314758f));
+  q = ffma2(q, f, pack_f32x2(0.9999282360076904f, 0.9999282360076904f));
+  float q0, q1, t0, t1;
+  unpack_f32x2(q, q0, q1);
+  unpack_f32x2(t, t0, t1);
+  y0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
 // Which K/V tile step j reads: chunk c, tile t within the chunk, valid rows.
 __device__ __forceinline__ void step_info(const AttnKernelParams& p, int j, int& c, int& t,
                                           int& valid, bool& extra) {
@@ -198,6 +240,7 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
     else
       tma_load_4d(smem + C::kOffK + ks * kTileBytes, tm_k, bar.k_full + ks, 0, t * kTile, bh, c);
     ++nk;
+    RP_TRACE(80, j);
     const int vs = j % kVSt, vu = j / kVSt;
     if (vu > 0 && !mbar_wait(bar.v_empty + vs, (vu - 1) & 1, bar.abort_flag, p.status,
                              kErrWaitVEmpty)) {
@@ -210,6 +253,7 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
     else
       tma_load_4d(smem + C::kOffV + vs * kTileBytes, tm_v, bar.v_full + vs, 0, t * kTile, bh, c);
     ++nv;
+    RP_TRACE(81, j);
   }
   if (!ok) {
     // Abort: let every load already issued land before shared memory goes away.
@@ -230,10 +274,12 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
   const int vsl = i % kVSt;
   if (!mbar_wait(bar.v_full + vsl, (i / kVSt) & 1, bar.abort_flag, p.status, kErrWaitV))
     return false;
+  RP_TRACE(71, i);
   const uint64_t vd = make_sw128_desc(sbase + C::kOffV + vsl * kTileBytes, kTileBytes, 1024);
 #pragma unroll
   for (int t = 0; t < NQ; ++t) {
     if (!mbar_wait(bar.p_full + t, i & 1, bar.abort_flag, p.status, kErrWaitP)) return false;
+    RP_TRACE(70 + 2 * t, i);
     tc_fence_after();
     const int pb = (C::kPBuf == 2) ? (i & 1) : 0;
     const uint32_t paddr = sbase + C::kOffP + (t * C::kPBuf + pb) * C::kPStride;
@@ -248,6 +294,7 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
       for (int k = 0; k < 4; ++k) mma_f8(d_tmem, pl + 2 * k, vd + 256 * k, idesc_pv, 1u);
     }
     mma_commit(bar.o_done + t);
+    RP_TRACE(60 + t, i);
   }
   mma_commit(bar.v_empty + vsl);
   return true;
@@ -266,6 +313,7 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
       ok = false;
       break;
     }
+    RP_TRACE(75, j);
     const uint64_t kd = make_sw128_desc(sbase + C::kOffK + ks * kTileBytes, 16, 1024);
 #pragma unroll
     for (int t = 0; t < NQ; ++t) {
@@ -280,6 +328,7 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
       for (int k = 0; k < 4; ++k)
         mma_f8(tmem + t * kTile, qd + 2 * k, kd + 2 * k, idesc_qk, k > 0 ? 1u : 0u);
       mma_commit(bar.s_full + t);
+      RP_TRACE(50 + t, j);
     }
     if (!ok) break;
     mma_commit(bar.k_empty + ks);
@@ -292,7 +341,7 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
 }
 
 // ----------------------------------------------------------------- softmax
-template <int NQ, int PMODE>
+template <int NQ, int PMODE, int EPOLY>
 __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
                            uint8_t* smem, uint32_t tmem, int n_steps) {
   using C = Cfg<NQ, PMODE>;
@@ -346,6 +395,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       ok = false;
       break;
     }
+    if (wq == 0 && lane == 0) RP_TRACE(10 + t, j);
     tc_fence_after();
     uint32_t r[4][32];
 #pragma unroll
@@ -379,26 +429,56 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         if (i < g0 || i > row) s[i] = -INFINITY;
     }
 
-    float mx = s[0];
+    // Row max: eight independent chains of 3-input max, then a short tree.
+    float a8[8];
 #pragma unroll
-    for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+    for (int k = 0; k < 8; ++k) {
+      float acc = s[16 * k];
+#pragma unroll
+      for (int jj = 0; jj < 7; ++jj) acc = fmax3f(acc, s[16 * k + 1 + 2 * jj], s[16 * k + 2 + 2 * jj]);
+      a8[k] = fmaxf(acc, s[16 * k + 15]);
+    }
+    const float mx =
+        fmax3f(fmax3f(a8[0], a8[1], a8[2]), fmax3f(a8[3], a8[4], a8[5]), fmaxf(a8[6], a8[7]));
     const float m_new = fmaxf(m_run, mx * cj);
     const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
     const float alpha = ex2_approx(m_run - m_use);
     const float noff = log2k - m_use;
 
+    // p' = 2^(s * c_j - m + log2 K_j).  Packed f32x2 FMAs form the exponents;
+    // EPOLY of every 8 go through the FMA-pipe polynomial, the rest through
+    // MUFU ex2; the row sum runs on four packed accumulators.
     uint32_t pk[32];
     uint32_t pl[(PMODE == 1) ? 32 : 1];
-    float sum = 0.f;
+    const uint64_t c2 = pack_f32x2(cj, cj);
+    const uint64_t o2 = pack_f32x2(noff, noff);
+    uint64_t sacc[4];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float e0 = ex2_approx(fmaf(s[4 * i + 0], cj, noff));
-      const float e1 = ex2_approx(fmaf(s[4 * i + 1], cj, noff));
-      const float e2 = ex2_approx(fmaf(s[4 * i + 2], cj, noff));
-      const float e3 = ex2_approx(fmaf(s[4 * i + 3], cj, noff));
-      sum += (e0 + e1) + (e2 + e3);
-      pk[i] = pack_e4m3x4(e0, e1, e2, e3);
-      if constexpr (PMODE == 1) pl[i] = pack_e4m3x4_residual(pk[i], e0, e1, e2, e3);
+    for (int i = 0; i < 16; ++i) {
+      float x[8], e[8];
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+        unpack_f32x2(ffma2(pack_f32x2(s[8 * i + 2 * h], s[8 * i + 2 * h + 1]), c2, o2), x[2 * h],
+                     x[2 * h + 1]);
+#pragma unroll
+      for (int k = 0; k < 8 - EPOLY; ++k) e[k] = ex2_approx(x[k]);
+#pragma unroll
+      for (int k = 8 - EPOLY; k < 8; k += 2) ex2_poly2(x[k], x[k + 1], e[k], e[k + 1]);
+      const uint64_t e8 = fadd2(fadd2(pack_f32x2(e[0], e[1]), pack_f32x2(e[2], e[3])),
+                                fadd2(pack_f32x2(e[4], e[5]), pack_f32x2(e[6], e[7])));
+      sacc[i & 3] = (i < 4) ? e8 : fadd2(sacc[i & 3], e8);
+      pk[2 * i] = pack_e4m3x4(e[0], e[1], e[2], e[3]);
+      pk[2 * i + 1] = pack_e4m3x4(e[4], e[5], e[6], e[7]);
+      if constexpr (PMODE == 1) {
+        pl[2 * i] = pack_e4m3x4_residual(pk[2 * i], e[0], e[1], e[2], e[3]);
+        pl[2 * i + 1] = pack_e4m3x4_residual(pk[2 * i + 1], e[4], e[5], e[6], e[7]);
+      }
+    }
+    float sum;
+    {
+      float u0, u1;
+      unpack_f32x2(fadd2(fadd2(sacc[0], sacc[1]), fadd2(sacc[2], sacc[3])), u0, u1);
+      sum = u0 + u1;
     }
 
     if (C::kPBuf == 1 && j > 0) {
@@ -420,6 +500,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
                      pl[4 * k + 2], pl[4 * k + 3]);
     }
     fence_proxy_async_smem();
+    if (wq == 0 && lane == 0) RP_TRACE(20 + t, j);
 
     if (j > 0) {
       if (C::kPBuf == 2 &&
@@ -427,15 +508,23 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         ok = false;
         break;
       }
+      if (wq == 0 && lane == 0) RP_TRACE(30 + t, j);
       tc_fence_after();
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        if (wq == 0 && lane == 0) RP_TRACE(90 + t, j);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint32_t o[32];
           tmem_ld32(tO + 32 * q, o);
           tmem_wait_ld();
+          const uint64_t a2 = pack_f32x2(alpha, alpha);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          for (int i = 0; i < 32; i += 2) {
+            float u0, u1;
+            unpack_f32x2(fmul2(pack_f32x2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), a2), u0, u1);
+            o[i] = __float_as_uint(u0);
+            o[i + 1] = __float_as_uint(u1);
+          }
           tmem_st32(tO + 32 * q, o);
         }
         tmem_wait_st();
@@ -444,6 +533,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(bar.p_full + t);
+    if (wq == 0 && lane == 0) RP_TRACE(40 + t, j);
     l_run = l_run * alpha + sum / kj;
     m_run = m_new;
   }
@@ -489,7 +579,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
 }
 
-template <int NQ, int PMODE>
+template <int NQ, int PMODE, int EPOLY>
 __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
@@ -550,7 +640,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
   } else if (warp == C::kMmaWarp) {
     if (lane == 0) mma_issuer<NQ, PMODE>(p, bar, smem, tmem, n_steps);
   } else {
-    softmax_wg<NQ, PMODE>(&tm_o, p, bar, smem, tmem, n_steps);
+    softmax_wg<NQ, PMODE, EPOLY>(&tm_o, p, bar, smem, tmem, n_steps);
   }
 
   tc_fence_before();
@@ -561,11 +651,11 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
   }
 }
 
-template <int NQ, int PMODE>
+template <int NQ, int PMODE, int EPOLY>
 cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
                            cudaStream_t st) {
   using C = Cfg<NQ, PMODE>;
-  auto kern = fa8_fwd_kernel<NQ, PMODE>;
+  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -582,14 +672,41 @@ cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, 
   return cudaGetLastError();
 }
 
+// Elements (of every 8) whose exp2 runs on the FMA pipe instead of MUFU.
+// REPERCEP_B200_EXP_POLY in {0, 2, 4} overrides the default (read once).
+int exp_poly_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_EXP_POLY");
+    if (!e) return kDefaultExpPoly;
+    const int x = std::atoi(e);
+    return (x == 0 || x == 2 || x == 4) ? x : kDefaultExpPoly;
+  }();
+  return v;
+}
+
 }  // namespace
+
+#ifdef RP_PIPELINE_TRACE
+extern "C" int rp_trace_setup(void* buf, int cta_x, int cta_y) {
+  uint32_t* b = static_cast<uint32_t*>(buf);
+  if (cudaMemcpyToSymbol(g_trace_buf, &b, sizeof(b)) != cudaSuccess) return -1;
+  if (cudaMemcpyToSymbol(g_trace_x, &cta_x, sizeof(int)) != cudaSuccess) return -1;
+  if (cudaMemcpyToSymbol(g_trace_y, &cta_y, sizeof(int)) != cudaSuccess) return -1;
+  return 0;
+}
+#endif
 
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
                              int nq, int p_mode, cudaStream_t st) {
-  if (nq == 2 && p_mode == 0) return launch_variant<2, 0>(maps, p, B, H, st);
-  if (nq == 2 && p_mode == 1) return launch_variant<2, 1>(maps, p, B, H, st);
-  if (nq == 1 && p_mode == 0) return launch_variant<1, 0>(maps, p, B, H, st);
-  if (nq == 1 && p_mode == 1) return launch_variant<1, 1>(maps, p, B, H, st);
+  const int ep = exp_poly_setting();
+  if (nq == 2 && p_mode == 0) {
+    if (ep == 2) return launch_variant<2, 0, 2>(maps, p, B, H, st);
+    if (ep == 4) return launch_variant<2, 0, 4>(maps, p, B, H, st);
+    return launch_variant<2, 0, 0>(maps, p, B, H, st);
+  }
+  if (nq == 2 && p_mode == 1) return launch_variant<2, 1, 0>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 0) return launch_variant<1, 0, 0>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 1) return launch_variant<1, 1, 0>(maps, p, B, H, st);
   return cudaErrorInvalidValue;
 }
 

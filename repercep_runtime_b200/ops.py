@@ -181,9 +181,14 @@ def fp8_attention(
     (``fp8_flash_attn_hopper.py:432-586``): bf16 in, default scale 1/sqrt(D),
     output in the query's dtype and layout.
     """
-    if q.shape != k.shape or q.shape != v.shape:
-        raise ValueError("MHA only: q, k, v must have the same shape")
-    qq, kq, vq = quantize_fp8((q, k, v), scale_mode=scale_mode, layout=layout)
+    qshape, kshape = bhsd_shape(q, layout), bhsd_shape(k, layout)
+    if k.shape != v.shape or qshape[:2] != kshape[:2] or qshape[3] != kshape[3]:
+        raise ValueError("q, k, v must share batch, heads and head_dim; k and v one shape")
+    if q.shape == k.shape:
+        qq, kq, vq = quantize_fp8((q, k, v), scale_mode=scale_mode, layout=layout)
+    else:  # cross-length attention: one quantize call for Q, one for K and V
+        (qq,) = quantize_fp8((q,), scale_mode=scale_mode, layout=layout)
+        kq, vq = quantize_fp8((k, v), scale_mode=scale_mode, layout=layout)
     return attention_fp8_quantized(
         qq, kq, vq, causal=causal, scale=scale, p_mode=p_mode, out=out, out_layout=layout
     )
