@@ -40,7 +40,8 @@ constexpr int kTile = 128;
 constexpr int kTileBytes = kTile * kTile;
 constexpr int kKSt = 3;
 constexpr int kVSt = 3;
-constexpr int kDefaultExpPoly = 0;
+constexpr int kDefaultExpPoly = 2;
+constexpr int kDefaultPingPong = 0;
 
 // Pipeline tracing (compiled in only with -DRP_PIPELINE_TRACE): one chosen CTA
 // records (SM clock, event << 16 | step) at every barrier hand-off of every
@@ -48,12 +49,13 @@ constexpr int kDefaultExpPoly = 0;
 #ifdef RP_PIPELINE_TRACE
 // Slot (event, step) of the traced CTA; plain stores, so recording does not
 // stall the recording thread.
-__device__ uint32_t* g_trace_buf;
-__device__ int g_trace_x;
-__device__ int g_trace_y;
-constexpr int kTraceSteps = 1024;
+__device__ uint32_t* g_trace_buf = nullptr;
+__device__ int g_trace_x = -1;
+__device__ int g_trace_y = -1;
+constexpr int kTraceSteps = 1024;  // events < 256
 __device__ __forceinline__ void trace_event(int ev, int j) {
-  if ((int)blockIdx.x != g_trace_x || (int)blockIdx.y != g_trace_y) return;
+  if (g_trace_buf == nullptr || (int)blockIdx.x != g_trace_x || (int)blockIdx.y != g_trace_y)
+    return;
   g_trace_buf[ev * kTraceSteps + (j & (kTraceSteps - 1))] = static_cast<uint32_t>(clock64());
 }
 #define RP_TRACE(ev, j) trace_event((ev), (j))
@@ -72,6 +74,8 @@ enum : int {
   kErrWaitP = 0x108,
   kErrWaitO = 0x109,
   kErrWaitEpi = 0x10A,
+  kErrWaitOFinal = 0x10B,
+  kErrWaitTok = 0x10C,
 };
 
 template <int NQ, int PMODE>
@@ -89,14 +93,14 @@ struct Cfg {
   static constexpr int kOffP = kOffV + kVSt * kTileBytes;
   static constexpr int kPStride = kPParts * kTileBytes;
   static constexpr int kOffBar = kOffP + NQ * kPBuf * kPStride;
-  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 5 * NQ + 1;
+  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 8;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Bars {
   uint64_t *q_full, *k_full, *k_empty, *v_full, *v_empty;
-  uint64_t *s_full, *s_free, *p_full, *o_done, *epi, *fin;
+  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *tok;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -112,24 +116,26 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   b.v_empty = b.v_full + kVSt;
   b.s_full = b.v_empty + kVSt;
   b.s_free = b.s_full + NQ;
-  b.p_full = b.s_free + NQ;
-  b.o_done = b.p_full + NQ;
-  b.epi = b.o_done + NQ;
+  b.p_full = b.s_free + NQ;  // [NQ][2]: step j uses p_full[2 t + (j & 1)]
+  b.o_done = b.p_full + 2 * NQ;
+  b.o_final = b.o_done + NQ;
+  b.epi = b.o_final + NQ;
   b.fin = b.epi + NQ;
-  b.tmem_slot = reinterpret_cast<uint32_t*>(b.fin + 1);
+  b.tok = b.fin + 1;  // [2][4]: exp-phase hand-over between paired warps
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.tok + 8);
   b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
   return b;
 }
 
-// Lane 0 waits, the warp follows.  Keeps every .sync.aligned tcgen05
-// instruction after the wait warp-convergent even when the wait aborts.
+// Every lane waits on the barrier (one try_wait instruction for the warp;
+// the loop stays convergent because all lanes read the same barrier word,
+// clock and abort flag), then a vote makes the outcome warp-uniform.  No
+// shuffle: on the softmax path every MIO-queue instruction would wait behind
+// the other warpgroup's MUFU stream.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int code) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, status, code) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
+  const bool ok = mbar_wait(bar, parity, abort_flag, status, code);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Time-bounded wait that ignores the abort flag: used to drain in-flight
@@ -268,7 +274,7 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
 // -------------------------------------------------------------- MMA issuer
 template <int NQ, int PMODE>
 __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& bar,
-                                         uint32_t sbase, uint32_t tmem, int i) {
+                                         uint32_t sbase, uint32_t tmem, int i, bool last) {
   using C = Cfg<NQ, PMODE>;
   constexpr uint32_t idesc_pv = make_idesc_e4m3(128, 128, 0, 1);
   const int vsl = i % kVSt;
@@ -278,7 +284,12 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
   const uint64_t vd = make_sw128_desc(sbase + C::kOffV + vsl * kTileBytes, kTileBytes, 1024);
 #pragma unroll
   for (int t = 0; t < NQ; ++t) {
-    if (!mbar_wait(bar.p_full + t, i & 1, bar.abort_flag, p.status, kErrWaitP)) return false;
+    // Two P_full barriers per tile, alternating by step: a softmax warpgroup
+    // that runs ahead can complete step i+1 before this wait for step i, and
+    // a single barrier would then be two phases ahead of the parity wait.
+    if (!mbar_wait(bar.p_full + 2 * t + (i & 1), (i >> 1) & 1, bar.abort_flag, p.status,
+                   kErrWaitP))
+      return false;
     RP_TRACE(70 + 2 * t, i);
     tc_fence_after();
     const int pb = (C::kPBuf == 2) ? (i & 1) : 0;
@@ -294,6 +305,7 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
       for (int k = 0; k < 4; ++k) mma_f8(d_tmem, pl + 2 * k, vd + 256 * k, idesc_pv, 1u);
     }
     mma_commit(bar.o_done + t);
+    if (last) mma_commit(bar.o_final + t);
     RP_TRACE(60 + t, i);
   }
   mma_commit(bar.v_empty + vsl);
@@ -332,16 +344,16 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
     }
     if (!ok) break;
     mma_commit(bar.k_empty + ks);
-    if (j > 0) ok = issue_pv<NQ, PMODE>(p, bar, sbase, tmem, j - 1);
+    if (j > 0) ok = issue_pv<NQ, PMODE>(p, bar, sbase, tmem, j - 1, false);
   }
-  if (ok && n_steps > 0) issue_pv<NQ, PMODE>(p, bar, sbase, tmem, n_steps - 1);
+  if (ok && n_steps > 0) issue_pv<NQ, PMODE>(p, bar, sbase, tmem, n_steps - 1, true);
   // Everything this thread issued must finish before TMEM is released.
   mma_commit(bar.fin);
   mbar_drain(bar.fin, 0);
 }
 
 // ----------------------------------------------------------------- softmax
-template <int NQ, int PMODE, int EPOLY>
+template <int NQ, int PMODE, int EPOLY, int PP>
 __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
                            uint8_t* smem, uint32_t tmem, int n_steps) {
   using C = Cfg<NQ, PMODE>;
@@ -371,13 +383,16 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   vbits = __reduce_max_sync(0xffffffffu, vbits);
   const float sv_max = __uint_as_float(vbits);
 
-  float m_run = -INFINITY, l_run = 0.f;
-  bool ok = true;
-  for (int j = 0; j < n_steps; ++j) {
+  const float inv_svmax = 1.f / sv_max;
+
+  // Per-step constants: c_j (log2-domain score scale), log2 K_j and 1/K_j
+  // (K_j = 448 * sv_j / sv_max, the P scale).  They are formed one step
+  // ahead, after the exp loop, and their scale loads two steps ahead, so no
+  // global load, division or MUFU op sits on the path between two steps.
+  auto load_step = [&](int j, float& sk, float& sv) {
     int c, tt, valid;
     bool extra;
     step_info(p, j, c, tt, valid, extra);
-    float sk, sv;
     if (extra) {
       const int idx = bh * p.kvx_bh + q_tile_c * p.kvx_blk;
       sk = p.ksx[idx];
@@ -387,9 +402,29 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       sk = p.ks[idx];
       sv = p.vs[idx];
     }
-    const float cj = p.sm_scale_log2 * sq * sk;
-    const float kj = 448.f * (sv / sv_max);
-    const float log2k = __log2f(kj);
+  };
+  float cj = 0.f, log2k = 0.f, invk = 0.f;
+  auto make_consts = [&](float sk, float sv, float& c_out, float& l_out, float& i_out) {
+    const float kj = 448.f * sv * inv_svmax;
+    c_out = p.sm_scale_log2 * sq * sk;
+    l_out = __log2f(kj);
+    i_out = __fdividef(1.f, kj);
+  };
+  float sk_n = 0.f, sv_n = 1.f;
+  if (n_steps > 0) {
+    float sk0, sv0;
+    load_step(0, sk0, sv0);
+    make_consts(sk0, sv0, cj, log2k, invk);
+  }
+  if (n_steps > 1) load_step(1, sk_n, sv_n);
+
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true;
+  for (int j = 0; j < n_steps; ++j) {
+    int c, tt, valid;
+    bool extra;
+    step_info(p, j, c, tt, valid, extra);
+    if (wq == 0 && lane == 0) RP_TRACE(100 + t, j);
 
     if (!warp_wait(bar.s_full + t, j & 1, bar.abort_flag, p.status, kErrWaitS)) {
       ok = false;
@@ -401,6 +436,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
 #pragma unroll
     for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, r[q]);
     tmem_wait_ld();
+    if (wq == 0 && lane == 0) RP_TRACE(104 + t, j);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(bar.s_free + t);
@@ -440,10 +476,25 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     }
     const float mx =
         fmax3f(fmax3f(a8[0], a8[1], a8[2]), fmax3f(a8[3], a8[4], a8[5]), fmaxf(a8[6], a8[7]));
+    if (wq == 0 && lane == 0) RP_TRACE(106 + t, j);
     const float m_new = fmaxf(m_run, mx * cj);
+    const bool grew = m_new > m_run;
     const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
     const float alpha = ex2_approx(m_run - m_use);
     const float noff = log2k - m_use;
+
+    // With PP (two query tiles), the exp phases of the two warps that share an
+    // SM sub-partition alternate: warpgroup 0's step j after warpgroup 1's
+    // step j-1, warpgroup 1's step j after warpgroup 0's step j.  While one
+    // warp streams its exps through MUFU the other does the rest of its step.
+    if constexpr (PP && NQ == 2) {
+      const bool need = (t == 1) || (j > 0);
+      const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
+      if (need && !warp_wait(bar.tok + 4 * t + wq, par, bar.abort_flag, p.status, kErrWaitTok)) {
+        ok = false;
+        break;
+      }
+    }
 
     // p' = 2^(s * c_j - m + log2 K_j).  Packed f32x2 FMAs form the exponents;
     // EPOLY of every 8 go through the FMA-pipe polynomial, the rest through
@@ -474,6 +525,16 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         pl[2 * i + 1] = pack_e4m3x4_residual(pk[2 * i + 1], e[4], e[5], e[6], e[7]);
       }
     }
+    if (wq == 0 && lane == 0) RP_TRACE(108 + t, j);
+    if constexpr (PP && NQ == 2) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar.tok + 4 * (1 - t) + wq);
+    }
+    // Next step's constants (their MUFU ops queue behind this step's exps and
+    // are consumed a whole step later), then the scale loads for step j+2.
+    float cj_n = cj, log2k_n = log2k, invk_n = invk;
+    if (j + 1 < n_steps) make_consts(sk_n, sv_n, cj_n, log2k_n, invk_n);
+    if (j + 2 < n_steps) load_step(j + 2, sk_n, sv_n);
     float sum;
     {
       float u0, u1;
@@ -502,7 +563,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     fence_proxy_async_smem();
     if (wq == 0 && lane == 0) RP_TRACE(20 + t, j);
 
-    if (j > 0) {
+    // O needs rescaling only when a row's running max grew; only then must
+    // PV(j-1) have finished before O is touched.  (P buffer j&1 is already
+    // free: S_full(j) was committed after PV(j-2) was issued.)
+    if (j > 0 && __any_sync(0xffffffffu, grew)) {
       if (C::kPBuf == 2 &&
           !warp_wait(bar.o_done + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
         ok = false;
@@ -510,7 +574,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       }
       if (wq == 0 && lane == 0) RP_TRACE(30 + t, j);
       tc_fence_after();
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      {
         if (wq == 0 && lane == 0) RP_TRACE(90 + t, j);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -532,14 +596,19 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(bar.p_full + t);
+    if (lane == 0) mbar_arrive(bar.p_full + 2 * t + (j & 1));
     if (wq == 0 && lane == 0) RP_TRACE(40 + t, j);
-    l_run = l_run * alpha + sum / kj;
+    l_run = l_run * alpha + sum * invk;
     m_run = m_new;
+    cj = cj_n;
+    log2k = log2k_n;
+    invk = invk_n;
   }
 
+  // The last PV of this tile signals o_final (single use, so the wait is
+  // unambiguous even though o_done phases were skipped above).
   if (ok && n_steps > 0)
-    ok = warp_wait(bar.o_done + t, (n_steps - 1) & 1, bar.abort_flag, p.status, kErrWaitO);
+    ok = warp_wait(bar.o_final + t, 0, bar.abort_flag, p.status, kErrWaitOFinal);
   if (!ok) return;
 
   // Epilogue: O * (sv_max / 448) / l -> bf16, staged as two 128x64 halves in
@@ -579,7 +648,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
 }
 
-template <int NQ, int PMODE, int EPOLY>
+template <int NQ, int PMODE, int EPOLY, int PP>
 __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
@@ -606,11 +675,14 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
     for (int t = 0; t < NQ; ++t) {
       mbar_init(bar.s_full + t, 1);
       mbar_init(bar.s_free + t, 4);
-      mbar_init(bar.p_full + t, 4);
+      mbar_init(bar.p_full + 2 * t, 4);
+      mbar_init(bar.p_full + 2 * t + 1, 4);
       mbar_init(bar.o_done + t, 1);
+      mbar_init(bar.o_final + t, 1);
       mbar_init(bar.epi + t, 4);
     }
     mbar_init(bar.fin, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(bar.tok + i, 1);
     *bar.abort_flag = 0;
     fence_barrier_init();
   }
@@ -640,7 +712,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
   } else if (warp == C::kMmaWarp) {
     if (lane == 0) mma_issuer<NQ, PMODE>(p, bar, smem, tmem, n_steps);
   } else {
-    softmax_wg<NQ, PMODE, EPOLY>(&tm_o, p, bar, smem, tmem, n_steps);
+    softmax_wg<NQ, PMODE, EPOLY, PP>(&tm_o, p, bar, smem, tmem, n_steps);
   }
 
   tc_fence_before();
@@ -651,11 +723,11 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
   }
 }
 
-template <int NQ, int PMODE, int EPOLY>
+template <int NQ, int PMODE, int EPOLY, int PP>
 cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
                            cudaStream_t st) {
   using C = Cfg<NQ, PMODE>;
-  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY>;
+  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, PP>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -684,6 +756,17 @@ int exp_poly_setting() {
   return v;
 }
 
+// Alternate the exp phases of the two softmax warpgroups (1) or let them
+// run freely (0).  REPERCEP_B200_PINGPONG overrides the default (read once).
+int pingpong_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_PINGPONG");
+    if (!e) return kDefaultPingPong;
+    return std::atoi(e) ? 1 : 0;
+  }();
+  return v;
+}
+
 }  // namespace
 
 #ifdef RP_PIPELINE_TRACE
@@ -699,14 +782,20 @@ extern "C" int rp_trace_setup(void* buf, int cta_x, int cta_y) {
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
                              int nq, int p_mode, cudaStream_t st) {
   const int ep = exp_poly_setting();
+  const int pp = pingpong_setting();
   if (nq == 2 && p_mode == 0) {
-    if (ep == 2) return launch_variant<2, 0, 2>(maps, p, B, H, st);
-    if (ep == 4) return launch_variant<2, 0, 4>(maps, p, B, H, st);
-    return launch_variant<2, 0, 0>(maps, p, B, H, st);
+    if (pp) {
+      if (ep == 2) return launch_variant<2, 0, 2, 1>(maps, p, B, H, st);
+      if (ep == 4) return launch_variant<2, 0, 4, 1>(maps, p, B, H, st);
+      return launch_variant<2, 0, 0, 1>(maps, p, B, H, st);
+    }
+    if (ep == 2) return launch_variant<2, 0, 2, 0>(maps, p, B, H, st);
+    if (ep == 4) return launch_variant<2, 0, 4, 0>(maps, p, B, H, st);
+    return launch_variant<2, 0, 0, 0>(maps, p, B, H, st);
   }
-  if (nq == 2 && p_mode == 1) return launch_variant<2, 1, 0>(maps, p, B, H, st);
-  if (nq == 1 && p_mode == 0) return launch_variant<1, 0, 0>(maps, p, B, H, st);
-  if (nq == 1 && p_mode == 1) return launch_variant<1, 1, 0>(maps, p, B, H, st);
+  if (nq == 2 && p_mode == 1) return launch_variant<2, 1, 0, 0>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 0) return launch_variant<1, 0, 0, 0>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 1) return launch_variant<1, 1, 0, 0>(maps, p, B, H, st);
   return cudaErrorInvalidValue;
 }
 

@@ -10,7 +10,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/repercep_b200.h"
+#include "repercep_b200.h"
 #include "internal.h"
 
 namespace {
