@@ -85,6 +85,23 @@ int rp_quant_fp8_e4m3(int num_tensors, const void* const* x, const int64_t* stri
                       int S, int D, int scale_mode, void* const* out, float* const* scales,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of rp_quant_fp8_e4m3 for RP_SCALE_PER_BH (no
+ * counterpart in the reference, which always allocates through PyTorch).
+ * For callers that cannot provide device memory beyond their inputs and
+ * outputs: e.g. a plugin whose host passes it only the tensors it reads and
+ * writes and whose memory pool forbids raw cudaMalloc.  The per-(b,h) scratch
+ * (one uint32 partial amax per 128-token chunk) lives in a fixed 1 MiB
+ * library-owned device array per device (held until exit); shapes needing
+ * more than 262144 slots (num_tensors * B * H * ceil(S/128)) are rejected
+ * with RP_ERR_WORKSPACE.  All calls on a device share that array: calls whose
+ * kernels may overlap on the GPU race and must be serialised (one stream).
+ * Each call writes every slot it reads, so no clearing is needed.  The first
+ * call on a device looks up the array's device address; make it before any
+ * stream capture.  Bytes and scales equal rp_quant_fp8_e4m3's. */
+int rp_quant_fp8_e4m3_noalloc(int num_tensors, const void* const* x, const int64_t* strides,
+                              int B, int H, int S, int D, void* const* out,
+                              float* const* scales, void* stream);
+
 /* FP8 attention forward, non-causal or causal (top-left aligned mask, as the
  * reference's offs_m >= offs_n).  q8 (B*H, Sq, D), k8/v8 (B*H, Skv, D) e4m3
  * contiguous; qs/ks/vs dequant scales in `scale_mode` layout; out bf16

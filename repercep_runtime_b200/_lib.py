@@ -62,6 +62,21 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_void_p,
         ],
     ),
+    "rp_quant_fp8_e4m3_noalloc": (
+        _c_int,
+        [
+            _c_int,
+            ctypes.POINTER(_c_void_p),
+            _c_i64_p,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            ctypes.POINTER(_c_void_p),
+            ctypes.POINTER(_c_void_p),
+            _c_void_p,
+        ],
+    ),
     "rp_attn_fp8_fwd": (
         _c_int,
         [_c_void_p] * 6

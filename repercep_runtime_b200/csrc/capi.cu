@@ -132,6 +132,18 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 }  // namespace
 
+namespace rp {
+int set_last_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+}  // namespace rp
+
 extern "C" {
 
 int rp_abi_version(void) { return RP_ABI_VERSION; }

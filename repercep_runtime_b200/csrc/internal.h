@@ -8,6 +8,9 @@
 
 namespace rp {
 
+// Records `fmt` as the calling thread's rp_last_error() message; returns code.
+int set_last_error(int code, const char* fmt, ...);
+
 // ------------------------------------------------------------- quantize
 constexpr int kQuantRows = 128;     // tokens per scale block / per CTA
 constexpr int kQuantThreads = 256;  // threads per quantize CTA
