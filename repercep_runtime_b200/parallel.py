@@ -1,0 +1,187 @@
+"""Multi-GPU execution of the FP8 attention path (one process per GPU).
+
+Two schemes (the reference has neither: it runs on one GPU and its diffusers
+bridge falls back to SDPA whenever a parallel config is set,
+src/repercep/attention/diffusers_backend.py:199-212):
+
+* **batch x head sharding** — (b, h) slices are independent; each rank takes
+  a contiguous run of them and no data crosses GPUs (``shard_bh``).
+* **context parallelism** (long video sequences) — every rank holds a
+  contiguous slice of the sequence for Q, K and V.  It quantises its K/V
+  slice to e4m3 with per-128-token-block scales, the ranks all-gather the
+  e4m3 K/V (1 byte/element on the wire instead of 2) and the scales over
+  NCCL, and each rank runs attention of its own queries against every
+  rank's K/V chunk in one kernel launch (``ContextParallelAttention``).
+  Slices are whole 128-token blocks (the last rank takes the remainder), so
+  every block and its scale are exactly those of the single-GPU per-block
+  layout and the result is bit-identical to the single-GPU one.  Each rank
+  owns complete query rows, so no partial outputs are exchanged.  Remote K/V
+  always lands in this GPU's memory before any kernel reads it.
+
+The collective is injected (``all_gather``), so the bookkeeping is testable
+with gloo ranks on CPU and an oracle in place of the kernel.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+BLOCK = 128
+
+
+# --------------------------------------------------------------- sharding
+def shard_bh(B: int, H: int, rank: int, world: int) -> tuple[int, int]:
+    """Half-open range [start, stop) of flattened (b*H + h) slices for ``rank``.
+
+    Slices are split as evenly as possible; ranks differ by at most one.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} / world {world}")
+    total = B * H
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    stop = start + base + (1 if rank < extra else 0)
+    return start, stop
+
+
+@dataclass(frozen=True)
+class SeqShard:
+    """One rank's slice of a context-parallel sequence."""
+
+    rank: int
+    world: int
+    seq_len: int
+    chunk_rows: int  # rows every rank's buffer holds (multiple of 128)
+    start: int  # first global row owned by this rank
+    rows: int  # rows actually owned (the last rank may own fewer)
+
+    @property
+    def last_rows(self) -> int:
+        """Valid rows in the last rank's chunk."""
+        return self.seq_len - (self.world - 1) * self.chunk_rows
+
+
+def seq_shard(seq_len: int, rank: int, world: int) -> SeqShard:
+    """Whole-block sequence split for context parallelism.
+
+    Every rank but the last owns ``chunk_rows`` rows (a multiple of 128); the
+    last owns the remainder.  Raises if the sequence is too short for
+    ``world`` non-empty shards.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} / world {world}")
+    blocks = -(-seq_len // BLOCK)
+    chunk_rows = -(-blocks // world) * BLOCK
+    last_rows = seq_len - (world - 1) * chunk_rows
+    if last_rows <= 0:
+        raise ValueError(f"sequence of {seq_len} tokens is too short for {world} shards")
+    start = rank * chunk_rows
+    rows = chunk_rows if rank < world - 1 else last_rows
+    return SeqShard(rank, world, seq_len, chunk_rows, start, rows)
+
+
+# ----------------------------------------------------- context parallelism
+AllGather = Callable[["object", "object"], None]  # (output, input) -> None
+
+
+def nccl_all_gather(group=None) -> AllGather:  # type: ignore[no-untyped-def]
+    """``torch.distributed.all_gather_into_tensor`` bound to ``group``."""
+    import torch.distributed as dist
+
+    def gather(out, inp):  # type: ignore[no-untyped-def]
+        dist.all_gather_into_tensor(out, inp, group=group)
+
+    return gather
+
+
+class ContextParallelAttention:
+    """FP8 attention with the sequence split across ranks.
+
+    ``__call__(q, k, v)`` takes this rank's (B, H, rows, D) bf16 shard (the
+    rows of ``seq_shard(seq_len, rank, world)``) and returns the bf16 output
+    rows for it.
+    """
+
+    def __init__(
+        self,
+        seq_len: int,
+        rank: int,
+        world: int,
+        all_gather: AllGather | None = None,
+        p_mode: int = 0,
+        scale: float | None = None,
+    ) -> None:
+        self.shard = seq_shard(seq_len, rank, world)
+        self.all_gather = all_gather
+        self.p_mode = p_mode
+        self.scale = scale
+
+    def gather_kv(self, k8, v8, ks, vs):  # type: ignore[no-untyped-def]
+        """Pad this rank's e4m3 K/V (BH, rows, D) and per-block scales to the
+        common chunk size and all-gather them; returns (n_chunks, BH, chunk_rows, D)
+        K and V and (n_chunks, BH, chunk_rows/128) scales."""
+        import torch
+
+        sh = self.shard
+        bh, rows, d = k8.shape
+        nblk = sh.chunk_rows // BLOCK
+        world = sh.world
+        # K, V and both scale tensors travel in one byte buffer per rank.
+        kv_bytes = bh * sh.chunk_rows * d
+        sc_bytes = bh * nblk * 4
+        send = torch.zeros(2 * kv_bytes + 2 * sc_bytes, dtype=torch.uint8, device=k8.device)
+        kv = send[: 2 * kv_bytes].view(2, bh, sh.chunk_rows, d)
+        kv[0, :, :rows].copy_(k8.reshape(bh, rows, d).view(torch.uint8))
+        kv[1, :, :rows].copy_(v8.reshape(bh, rows, d).view(torch.uint8))
+        sc = send[2 * kv_bytes :].view(torch.float32).view(2, bh, nblk)
+        sc[:, :, : ks.shape[-1]].copy_(torch.stack([ks.reshape(bh, -1), vs.reshape(bh, -1)]))
+        recv = torch.empty(world * send.numel(), dtype=torch.uint8, device=k8.device)
+        if self.all_gather is None:
+            raise RuntimeError("no all_gather bound (world > 1 needs a process group)")
+        self.all_gather(recv, send)
+        per = recv.view(world, -1)
+        kvs = per[:, : 2 * kv_bytes].reshape(world, 2, bh, sh.chunk_rows, d)
+        scs = per[:, 2 * kv_bytes :].contiguous().view(torch.float32).reshape(world, 2, bh, nblk)
+        k_all = kvs[:, 0].contiguous()
+        v_all = kvs[:, 1].contiguous()
+        return k_all, v_all, scs[:, 0].contiguous(), scs[:, 1].contiguous()
+
+    def __call__(self, q, k, v, out=None):  # type: ignore[no-untyped-def]
+        import torch
+
+        from repercep_runtime_b200 import ops
+
+        sh = self.shard
+        if q.shape[2] != sh.rows or k.shape != q.shape or v.shape != q.shape:
+            raise ValueError(f"expected (B, H, {sh.rows}, D) shards for rank {sh.rank}")
+        qq, kq, vq = ops.quantize_fp8((q, k, v), scale_mode=ops.SCALE_PER_BLOCK128)
+        if sh.world == 1:
+            return ops.attention_fp8_quantized(qq, kq, vq, scale=self.scale, p_mode=self.p_mode, out=out)
+        B, H, rows, D = q.shape
+        k_all, v_all, ks_all, vs_all = self.gather_kv(
+            kq.data.view(torch.uint8).reshape(B * H, rows, D),
+            vq.data.view(torch.uint8).reshape(B * H, rows, D),
+            kq.scales,
+            vq.scales,
+        )
+        return ops.attention_fp8_chunked(
+            qq,
+            k_all.view(ops.FP8),
+            v_all.view(ops.FP8),
+            ks_all,
+            vs_all,
+            last_rows=sh.last_rows,
+            scale=self.scale,
+            p_mode=self.p_mode,
+            out=out,
+        )
+
+
+__all__ = [
+    "ContextParallelAttention",
+    "SeqShard",
+    "nccl_all_gather",
+    "seq_shard",
+    "shard_bh",
+]

@@ -1,0 +1,76 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point the
+header declares, and its argument checks fail cleanly before any device work."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from repercep_runtime_b200 import _lib
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from repercep_runtime_b200 import build
+
+    build.build()  # no-op when up to date; nvcc cross-compiles without a GPU
+    return _lib.load()
+
+
+def _declared_symbols() -> set[str]:
+    text = _lib.HEADER_PATH.read_text()
+    return set(re.findall(r"^\s*(?:int|const char\*)\s+(rp_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_declares_the_expected_entry_points():
+    syms = _declared_symbols()
+    for name in ("rp_quant_fp8_e4m3", "rp_quant_fp8_e4m3_noalloc", "rp_attn_fp8_fwd",
+                 "rp_attn_fp8_fwd_chunked", "rp_attn_fp8_prefix_decode", "rp_last_error"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in sorted(_declared_symbols()):
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_abi_version(lib):
+    assert lib.rp_abi_version() == _lib.ABI_VERSION
+
+
+def test_workspace_size_is_host_only(lib):
+    n = ctypes.c_size_t(0)
+    assert lib.rp_quant_workspace_bytes(3, 2, 32, 8192, 128, 0, ctypes.byref(n)) == 0
+    assert n.value == 3 * 2 * 32 * 64 * 4
+    assert lib.rp_quant_workspace_bytes(3, 2, 32, 8192, 128, 1, ctypes.byref(n)) == 0
+    assert n.value == 0
+    assert lib.rp_quant_workspace_bytes(3, 2, 32, 8192, 128, 7, ctypes.byref(n)) == -1
+
+
+def test_argument_errors_are_reported_not_thrown(lib):
+    strides = _lib.i64_array([0, 0, 0, 1])
+    ptrs = _lib.ptr_array([0])
+    rc = lib.rp_quant_fp8_e4m3(4, ptrs, strides, 1, 1, 1, 128, 0, ptrs, ptrs, None, 0, None)
+    assert rc == -1 and b"num_tensors" in lib.rp_last_error()
+    rc = lib.rp_quant_fp8_e4m3(1, ptrs, strides, 1, 1, 1, 96, 0, ptrs, ptrs, None, 0, None)
+    assert rc == -2 and b"head_dim" in lib.rp_last_error()
+    out_strides = _lib.i64_array([1, 1, 1, 1])
+    rc = lib.rp_attn_fp8_fwd(None, None, None, None, None, None, 0, 1, 1, 128, 128, 128, 0.0, 0, 0,
+                             None, out_strides, None)
+    assert rc == -1 and b"null" in lib.rp_last_error()
+    dummy = 1 << 20
+    rc = lib.rp_attn_fp8_fwd(dummy, dummy, dummy, dummy, dummy, dummy, 0, 1, 1, 128, 128, 64, 0.0, 0,
+                             0, dummy, out_strides, None)
+    assert rc == -2 and b"head_dim" in lib.rp_last_error()
+    rc = lib.rp_attn_fp8_prefix_decode(*([dummy] * 10), 4, 3, 512, 32, 128, 0.0, 0, dummy,
+                                       _lib.i64_array([1, 1, 1]), None)
+    assert rc == -2 and b"divide 128" in lib.rp_last_error()
+
+
+def test_native_error_carries_the_message(lib):
+    with pytest.raises(_lib.NativeError, match="RP_ERR_INVALID"):
+        _lib.check("rp_quant_workspace_bytes",
+                   lib.rp_quant_workspace_bytes(0, 1, 1, 1, 1, 0, ctypes.byref(ctypes.c_size_t())))

@@ -1,0 +1,104 @@
+"""The oracle against the reference's own outputs (tests/golden, produced by
+tests/golden/make_golden.py from the reference source tree)."""
+
+from __future__ import annotations
+
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from helpers import bytes_equal_nan_aware, scales_equal
+from oracle import attention as oa
+from oracle import quantize as oq
+from oracle.fp8 import bf16_bits_to_f32, e4m3_decode, e4m3_encode, f32_to_bf16_bits
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _cases(fname: str) -> dict[str, dict[str, np.ndarray]]:
+    data = np.load(GOLDEN / fname)
+    out: dict[str, dict[str, np.ndarray]] = {}
+    for key in data.files:
+        case, field = key.split("/")
+        out.setdefault(case, {})[field] = data[key]
+    return out
+
+
+QUANT = _cases("quantize_cases.npz")
+ATTN = _cases("attention_cases.npz")
+
+
+@pytest.mark.parametrize("name", sorted(QUANT))
+def test_oracle_quantize_matches_reference_bytes(name):
+    c = QUANT[name]
+    q, s = oq.quantize_with_scales(c["x"], oq.SCALE_PER_BH)
+    assert scales_equal(s, c["scales"]).all()
+    assert (q == c["q"]).all(), f"{(q != c['q']).sum()} bytes differ"  # NaN bytes included
+
+
+@pytest.mark.parametrize("name", sorted(ATTN))
+def test_oracle_tile_loop_matches_reference_kernel(name):
+    """The restated FA-2 loop (P rounded as e4m3(p*448), natural exp) equals
+    the reference kernel's bf16 output bit for bit."""
+    c = ATTN[name]
+    B, H, S, D = c["q"].shape
+    causal = bool(c["causal"][0])
+    q8, qs = oq.quantize_with_scales(c["q"], oq.SCALE_PER_BH)
+    k8, ks = oq.quantize_with_scales(c["k"], oq.SCALE_PER_BH)
+    v8, vs = oq.quantize_with_scales(c["v"], oq.SCALE_PER_BH)
+    got = oa.reference_tile_loop(
+        q8.reshape(B * H, S, D), k8.reshape(B * H, S, D), v8.reshape(B * H, S, D), qs, ks, vs,
+        1 / math.sqrt(D), causal=causal,
+    )
+    assert (f32_to_bf16_bits(got).reshape(c["out"].shape) == c["out"]).all()
+
+
+@pytest.mark.parametrize("name", sorted(ATTN))
+def test_reference_kernel_within_tolerance_of_dequant_attention(name):
+    """The contract the B200 kernel is held to, checked on the reference
+    kernel itself: cosine >= 0.999 against fp32 attention on the same
+    dequantised inputs (max-abs relative to the output range)."""
+    c = ATTN[name]
+    B, H, S, D = c["q"].shape
+    causal = bool(c["causal"][0])
+    q8, qs = oq.quantize_with_scales(c["q"], oq.SCALE_PER_BH)
+    k8, ks = oq.quantize_with_scales(c["k"], oq.SCALE_PER_BH)
+    v8, vs = oq.quantize_with_scales(c["v"], oq.SCALE_PER_BH)
+    ref = oa.attention_dequant(
+        q8.reshape(B * H, S, D), k8.reshape(B * H, S, D), v8.reshape(B * H, S, D), qs, ks, vs,
+        1 / math.sqrt(D), causal=causal,
+    )
+    m = oa.parity_metrics(bf16_bits_to_f32(c["out"]).reshape(B * H, S, D), ref)
+    assert m["cos"] >= 0.999, m
+    # rows of the causal case that see few keys do not average P's rounding
+    bound = 0.02 * m["max_ref"] if causal else 2e-2
+    assert m["max_abs"] <= bound, m
+
+
+def test_e4m3_codec_roundtrip_all_bytes():
+    b = np.arange(256, dtype=np.uint8)
+    vals = e4m3_decode(b)
+    finite = ~np.isnan(vals)
+    back = e4m3_encode(vals[finite].astype(np.float32))
+    assert (back == b[finite]).all()
+    assert np.isnan(vals).sum() == 2  # 0x7F and 0xFF
+
+
+def test_bf16_rounding_ties_to_even():
+    x = np.array([1.0 + 2.0**-8, 1.0 + 3 * 2.0**-8, -1.0 - 2.0**-8], dtype=np.float32)
+    assert bf16_bits_to_f32(f32_to_bf16_bits(x)).tolist() == [1.0, 1.0 + 2.0**-6, -1.0]
+    assert f32_to_bf16_bits(np.array([np.nan], np.float32))[0] == 0x7FC0
+
+
+def test_per_block_mode_equals_per_bh_on_a_single_block():
+    rng = np.random.default_rng(0)
+    x = f32_to_bf16_bits(rng.standard_normal((1, 2, 100, 64)).astype(np.float32)).reshape(1, 2, 100, 64)
+    qa, sa = oq.quantize_with_scales(x, oq.SCALE_PER_BH)
+    qb, sb = oq.quantize_with_scales(x, oq.SCALE_PER_BLOCK128)
+    assert (qa == qb).all() and (sa == sb[:, 0]).all()
+
+
+def test_quantize_oracle_nan_aware_helper():
+    assert bytes_equal_nan_aware(np.array([0x7F], np.uint8), np.array([0xFF], np.uint8)).all()

@@ -1,0 +1,106 @@
+"""Multi-GPU host logic on CPU: batch x head sharding, the whole-block
+sequence split, and the context-parallel K/V gather run as two gloo ranks with
+the oracle standing in for the kernel."""
+
+from __future__ import annotations
+
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from repercep_runtime_b200.parallel import ContextParallelAttention, seq_shard, shard_bh
+
+
+@pytest.mark.parametrize("B,H,world", [(2, 32, 1), (2, 32, 8), (2, 40, 8), (1, 3, 2), (2, 5, 4)])
+def test_shard_bh_partitions_every_slice_once(B, H, world):
+    seen = []
+    for r in range(world):
+        a, b = shard_bh(B, H, r, world)
+        seen.extend(range(a, b))
+        assert (b - a) in (B * H // world, B * H // world + 1)
+    assert seen == list(range(B * H))
+
+
+@pytest.mark.parametrize("S,world", [(75600, 2), (75600, 4), (75600, 8), (57600, 8), (300, 2), (128, 1)])
+def test_seq_shard_is_whole_blocks_and_covers_the_sequence(S, world):
+    rows = []
+    for r in range(world):
+        sh = seq_shard(S, r, world)
+        assert sh.chunk_rows % 128 == 0
+        assert sh.start % 128 == 0
+        rows.extend(range(sh.start, sh.start + sh.rows))
+    assert rows == list(range(S))
+    assert seq_shard(S, world - 1, world).rows == seq_shard(S, 0, world).last_rows
+
+
+def test_seq_shard_rejects_too_short():
+    with pytest.raises(ValueError, match="too short"):
+        seq_shard(200, 3, 4)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cp_worker(rank: int, world: int, port: int, S: int) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from helpers import bits, gen_bf16
+        from oracle import attention as oa
+        from oracle import quantize as oq
+
+        B, H, D = 1, 2, 64
+        full = [gen_bf16((B, H, S, D), "n1", 40 + i) for i in range(3)]
+        cp = ContextParallelAttention(
+            S, rank, world, all_gather=lambda o, i: dist.all_gather_into_tensor(o, i)
+        )
+        sh = cp.shard
+        local = [t[:, :, sh.start : sh.start + sh.rows] for t in full]
+        # this rank's K/V quantised per block (the oracle in place of the CUDA quantizer)
+        k8, ks = oq.quantize_with_scales(bits(local[1]), oq.SCALE_PER_BLOCK128)
+        v8, vs = oq.quantize_with_scales(bits(local[2]), oq.SCALE_PER_BLOCK128)
+        k_all, v_all, ks_all, vs_all = cp.gather_kv(
+            torch.from_numpy(k8.reshape(B * H, sh.rows, D)),
+            torch.from_numpy(v8.reshape(B * H, sh.rows, D)),
+            torch.from_numpy(ks),
+            torch.from_numpy(vs),
+        )
+        assert k_all.shape == (world, B * H, sh.chunk_rows, D)
+        # the gathered chunks, trimmed to their valid rows, are the global per-block layout
+        kg = np.concatenate(
+            [k_all[c, :, : (sh.chunk_rows if c < world - 1 else sh.last_rows)].numpy() for c in range(world)], 1
+        )
+        vg = np.concatenate(
+            [v_all[c, :, : (sh.chunk_rows if c < world - 1 else sh.last_rows)].numpy() for c in range(world)], 1
+        )
+        nb = lambda c: sh.chunk_rows // 128 if c < world - 1 else -(-sh.last_rows // 128)  # noqa: E731
+        ksg = np.concatenate([ks_all[c, :, : nb(c)].numpy() for c in range(world)], 1)
+        vsg = np.concatenate([vs_all[c, :, : nb(c)].numpy() for c in range(world)], 1)
+        kf, ksf = oq.quantize_with_scales(bits(full[1]), oq.SCALE_PER_BLOCK128)
+        vf, vsf = oq.quantize_with_scales(bits(full[2]), oq.SCALE_PER_BLOCK128)
+        assert (kg == kf.reshape(B * H, S, D)).all() and (vg == vf.reshape(B * H, S, D)).all()
+        assert (ksg == ksf).all() and (vsg == vsf).all()
+        # attention of this rank's rows over the gathered K/V == the same rows of the full problem
+        q8, qs = oq.quantize_with_scales(bits(full[0]), oq.SCALE_PER_BLOCK128)
+        rows = np.arange(sh.start, sh.start + sh.rows)
+        got = oa.attention_dequant(q8.reshape(B * H, S, D), kg, vg, qs, ksg, vsg, 1 / math.sqrt(D), rows=rows)
+        ref = oa.attention_dequant(q8.reshape(B * H, S, D), kf.reshape(B * H, S, D), vf.reshape(B * H, S, D),
+                                   qs, ksf, vsf, 1 / math.sqrt(D), rows=rows)
+        assert np.array_equal(got, ref)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("S,world", [(300, 2), (512, 2)])
+def test_context_parallel_gather_with_gloo_ranks(S, world):
+    mp.spawn(_cp_worker, args=(world, _free_port(), S), nprocs=world, join=True)
