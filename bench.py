@@ -6,18 +6,23 @@
 
 One *step* is one pass of the hot path over one batch: quantize Q, K, V
 (bf16 -> e4m3 + scales) and run the FP8 attention kernel (bf16 out) — the
-work of the reference's ``fp8_flash_attention`` call.  Default workload:
-the Cosmos-shaped attention (B=2, H=32, S=57600, D=128, N(0,0.5), per-128-
-token-block scales).  Metric: algorithmic TFLOP/s (4*B*H*S^2*D per call),
-whole-job aggregate over N GPUs, device-timed with CUDA events, max over
-ranks.  Multi-GPU: batch x head slices shard across ranks with no
-collective on the data path (weak scaling by default: every rank runs a full
-Cosmos-shaped call on its own slices).
+work of the reference's ``fp8_flash_attention`` call.  Default workload: the
+Cosmos-shaped attention (B=2, H=32, S=57600, D=128, N(0,0.5), per-128-token
+block scales).  Metric: algorithmic TFLOP/s (4*B*H*Sq*Skv*D per call), whole
+job aggregate over N GPUs, device-timed with CUDA events, max over ranks.
+
+Multi-GPU (one process per GPU under torchrun):
+  cosmos / cfg2  batch x head slices shard across ranks with no collective;
+                 weak scaling by default (every rank a full call's worth of
+                 slices), --scaling strong splits one call's slices.
+  wan            context parallelism: the sequence splits across ranks, e4m3
+                 K/V is all-gathered over NCCL (strong scaling).
+  decode         shared-prefix candidate decode, independent replicas.
 
 ``--impl reference`` times the reference's own CPU attention (its AMX BF16
 flash kernel, built from its source into oracle/_ref; the numpy oracle when
-that cannot run) on a bounded sample of the same workload on the host cores.
-Rank 0 prints one JSON line.
+that cannot run) on a bounded sample of the same workload on the host cores;
+under torchrun only rank 0 runs it.  Rank 0 prints one JSON line.
 """
 
 from __future__ import annotations
@@ -41,37 +46,42 @@ UNIT = "TFLOP/s"
 FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense e4m3, per GPU (nominal)
 
 WORKLOADS = {
-    "cosmos": dict(B=2, H=32, S=57600, D=128, dist="n05", scale_mode=1,
+    "cosmos": dict(kind="attn", B=2, H=32, S=57600, D=128, dist="n05", scale_mode=1,
                    desc="Cosmos-7B DiT self-attn, 16x45x80 patches, N(0,0.5), per-128-block scales"),
-    "cfg2": dict(B=2, H=32, S=8192, D=128, dist="n1_outlier", scale_mode=0,
+    "cfg2": dict(kind="attn", B=2, H=32, S=8192, D=128, dist="n1_outlier", scale_mode=0,
                  desc="B=2 H=32 S=8192, N(0,1) with 1% x20 outliers, per-(b,h) scales"),
-    "wan": dict(B=2, H=40, S=75600, D=128, dist="n05", scale_mode=1,
-                desc="Wan-2.2 DiT self-attn, 21x45x80 patches, N(0,0.5), per-128-block scales"),
+    "wan": dict(kind="attn", B=2, H=40, S=75600, D=128, dist="n05", scale_mode=1,
+                desc="Wan-2.2 DiT self-attn, 21x45x80 patches, N(0,0.5), per-128-block scales; "
+                     "context parallel over N GPUs"),
+    "decode": dict(kind="decode", C=64, T=8, H=32, P=512, D=128, dist="n1",
+                   desc="token-VLA shared-prefix decode: 64 candidates x 8 new tokens, 512-token "
+                        "prefix (quantised once, e4m3-resident), causal per-candidate suffix"),
+    "plumbing": dict(kind="cpu", B=1, H=8, S=1024, D=64, dist="n1", scale_mode=0,
+                     desc="CPU plumbing case: B=1 H=8 S=1024 D=64, N(0,1) (reference CPU path only)"),
 }
 
 
 def flops_per_call(w: dict) -> float:
+    if w["kind"] == "decode":
+        rows = w["C"] * w["T"]
+        pairs = rows * w["P"] + w["C"] * w["T"] * (w["T"] + 1) // 2
+        return 4.0 * w["H"] * pairs * w["D"]
     return 4.0 * w["B"] * w["H"] * w["S"] * w["S"] * w["D"]
 
 
 # ------------------------------------------------------------------ helpers
-def gen_inputs(w: dict, seed: int, device: str):
-    """Seeded synthetic bf16 Q, K, V on `device` (Q=seed, K=seed+1, V=seed+2)."""
+def gen_tensor(shape, dist: str, seed: int, device: str):
+    """Seeded synthetic bf16 tensor on `device`."""
     import torch
 
-    shape = (w["B"], w["H"], w["S"], w["D"])
-    out = []
-    for i in range(3):
-        g = torch.Generator(device=device).manual_seed(seed + i)
-        x = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
-        if w["dist"] == "n05":
-            x.mul_(0.5)
-        elif w["dist"] == "n1_outlier":
-            mask = torch.rand(shape, generator=g, device=device) < 0.01
-            x = torch.where(mask, x * 20.0, x)
-        out.append(x.to(torch.bfloat16))
-        del x
-    return out
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+    if dist == "n05":
+        x.mul_(0.5)
+    elif dist == "n1_outlier":
+        mask = torch.rand(shape, generator=g, device=device) < 0.01
+        x = torch.where(mask, x * 20.0, x)
+    return x.to(torch.bfloat16)
 
 
 def load_peaks() -> dict:
@@ -85,7 +95,7 @@ def load_peaks() -> dict:
 
 
 def profile_traffic(workload: str) -> float | None:
-    """DRAM bytes per attention launch, from the committed ncu summary."""
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
     p = REPO / "profiles" / f"fa8_fwd_{workload}.txt"
     if not p.exists():
         return None
@@ -137,6 +147,10 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        return self.parse(out)
+
+    @classmethod
+    def parse(cls, out: str) -> dict | None:
         sm, mx, reasons = [], [], set()
         for line in out.splitlines():
             parts = [p.strip() for p in line.split(",")]
@@ -147,17 +161,13 @@ class ClockSampler:
                 mx.append(float(parts[1]))
             except ValueError:
                 continue
-            for name, val in zip(self.REASONS, parts[3:7]):
+            for name, val in zip(cls.REASONS, parts[3:7]):
                 if val.lower() == "active":
                     reasons.add(name)
         if not sm:
             return None
-        return {
-            "sm_mhz": statistics.median(sm),
-            "sm_max_mhz": max(mx),
-            "reasons": sorted(reasons),
-            "samples": len(sm),
-        }
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -166,53 +176,62 @@ def cpu_reference_sample(w: dict, target_s: float = 8.0) -> dict:
 
     The reference's CPU path is bf16 (it has no FP8; src/repercep/backend/cpu.py:264).
     Kind "reference": its AMX flash kernel (kernels/cpu/amx_attn/flash_attn_amx.cpp,
-    built into oracle/_ref) on whole (b,h) slices at the full sequence length.
-    Kind "port": the numpy oracle on a few query rows of one slice.
+    built into oracle/_ref) on one (b,h) slice at the full sequence length (the
+    whole problem for the plumbing case).  Kind "port": the numpy oracle on a few
+    query rows of one slice.  Decode: the prefix+suffix attention of one head.
     """
     import torch
 
     from oracle.build_ref import load_reference_kernel
 
-    S, D = w["S"], w["D"]
     g = torch.Generator().manual_seed(7)
-    cores = torch.get_num_threads()
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    if w["kind"] == "decode":
+        S, D, bh, label = w["P"] + w["C"] * w["T"], w["D"], 1, "one head of the decode (prefix+suffix keys)"
+        flops = flops_per_call(w) / w["H"]
+    else:
+        D = w["D"]
+        S = w["S"]
+        bh = w["B"] * w["H"] if w["kind"] == "cpu" else 1
+        flops = 4.0 * bh * S * S * D
+        label = "the whole call" if bh > 1 else f"1 (b,h) slice of {w['B'] * w['H']}"
     mod = None
     try:
         mod = load_reference_kernel()
     except Exception:
         mod = None
     if mod is not None and S % 32 == 0 and D in (64, 128):
-        q, k, v = (torch.randn((1, 1, S, D), generator=g).mul_(0.5).to(torch.bfloat16) for _ in range(3))
+        B, H = (w["B"], w["H"]) if w["kind"] == "cpu" else (1, 1)
+        q, k, v = (torch.randn((B, H, S, D), generator=g).to(torch.bfloat16) for _ in range(3))
         sm = 1.0 / math.sqrt(D)
-        mod.flash_attn_bf16(q[:, :, :128].contiguous(), k[:, :, :128].contiguous(), v[:, :, :128].contiguous(), sm, False)
+        mod.flash_attn_bf16(q, k, v, sm, False)
         t0 = time.perf_counter()
         mod.flash_attn_bf16(q, k, v, sm, False)
         one = time.perf_counter() - t0
-        reps = max(1, min(8, int(target_s / max(one, 1e-3))))
+        reps = max(1, min(20, int(target_s / max(one, 1e-3))))
         t0 = time.perf_counter()
         for _ in range(reps):
             mod.flash_attn_bf16(q, k, v, sm, False)
         dt = (time.perf_counter() - t0) / reps
-        flops = 4.0 * S * S * D
+        flops_sample = 4.0 * B * H * S * S * D
         return {
-            "value": flops / dt / 1e12,
+            "value": flops_sample / dt / 1e12,
             "unit": UNIT,
-            "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or cores)),
+            "cores": cores,
             "kind": "reference",
-            "sample": f"reference AMX bf16 flash kernel, 1 (b,h) slice at full S={S}, D={D}, {reps} calls "
-                      f"({dt * 1e3:.0f} ms each); scaled from 1 of {w['B'] * w['H']} slices",
+            "sample": f"reference AMX bf16 flash kernel (kernels/cpu/amx_attn), {label} at S={S}, "
+                      f"D={D}: {reps} calls of {dt * 1e3:.1f} ms",
             "seconds_per_sample": dt,
         }
-    # numpy oracle port (single process; BLAS threads)
     import numpy as np
 
     from oracle.attention import softmax_attention
 
-    rows = 256
+    rows = min(256, S)
     rng = np.random.default_rng(7)
-    qn = (rng.standard_normal((rows, D)) * 0.5).astype(np.float32)
-    kn = (rng.standard_normal((S, D)) * 0.5).astype(np.float32)
-    vn = (rng.standard_normal((S, D)) * 0.5).astype(np.float32)
+    qn = rng.standard_normal((rows, D)).astype(np.float32)
+    kn = rng.standard_normal((S, D)).astype(np.float32)
+    vn = rng.standard_normal((S, D)).astype(np.float32)
     t0 = time.perf_counter()
     softmax_attention(qn, kn, vn, 1 / math.sqrt(D))
     dt = time.perf_counter() - t0
@@ -221,151 +240,292 @@ def cpu_reference_sample(w: dict, target_s: float = 8.0) -> dict:
         "unit": UNIT,
         "cores": torch.get_num_threads(),
         "kind": "port",
-        "sample": f"numpy oracle attention, {rows} query rows x S={S} keys of 1 (b,h) slice",
+        "sample": f"numpy oracle attention, {rows} query rows x {S} keys of one slice",
         "seconds_per_sample": dt,
     }
+
+
+def config_for(args, w: dict, world: int) -> dict:
+    cfg = {"workload": args.workload, "desc": w["desc"], "flops_per_call": flops_per_call(w)}
+    if w["kind"] == "decode":
+        cfg.update(candidates=w["C"], new_tokens=w["T"], heads=w["H"], prefix=w["P"], head_dim=w["D"],
+                   parallelism=f"replicas x{world}")
+        return cfg
+    bh = w["B"] * w["H"]
+    cfg.update(batch=w["B"], heads=w["H"], seq_len=w["S"], head_dim=w["D"],
+               scale_mode="per_block128" if w["scale_mode"] == 1 else "per_bh",
+               p_mode="hilo" if args.p_mode == 1 else "e4m3")
+    if w["kind"] == "attn":
+        mode = parallel_mode(args, w, world)
+        if mode == "cp":
+            cfg.update(parallelism=f"context-parallel x{world} (NCCL all-gather of e4m3 K/V)")
+        else:
+            cfg.update(parallelism=f"bh-shard x{world}",
+                       global_bh=bh * world if args.scaling == "weak" else bh,
+                       per_rank_bh=bh if args.scaling == "weak" else -(-bh // world))
+        cfg["l2"] = "inputs (3 x %.2f GB bf16) exceed the 126 MB L2; no flush needed" % (
+            w["B"] * w["H"] * w["S"] * w["D"] * 2 / 1e9)
+    return cfg
+
+
+def parallel_mode(args, w: dict, world: int) -> str:
+    if w["kind"] != "attn" or world == 1:
+        return "single"
+    return "cp" if args.workload == "wan" else "shard"
 
 
 def run_reference_arm(args, w: dict, rank: int, world: int) -> None:
     if rank != 0:
         return
     base = cpu_reference_sample(w, target_s=2.0)
-    times = []
+    vals = []
     for i in range(args.warmup + args.steps):
         r = cpu_reference_sample(w, target_s=0.0)
         if i >= args.warmup:
-            times.append(r["value"])
-    value = statistics.mean(times) if times else base["value"]
-    flops = flops_per_call(w)
-    ms_call = flops / (value * 1e12) * 1e3
+            vals.append(r["value"])
+    value = statistics.mean(vals) if vals else base["value"]
+    ms_call = flops_per_call(w) / (value * 1e12) * 1e3
     line = {
-        "metric": METRIC,
-        "value": value,
-        "unit": UNIT,
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms_call,
-        "higher_is_better": True,
-        "scaling": args.scaling,
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic",
-        "impl": "reference",
-        "config": config_for(args, w, world),
-        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")} | {"value": value},
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_call, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "impl": "reference", "config": config_for(args, w, world),
+        "cpu_baseline": {k: base[k] for k in ("unit", "cores", "kind", "sample")} | {"value": value},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
-        "note": "each step times one bounded sample (one (b,h) slice at full S) on the host cores; "
-                "ms_per_step is the extrapolated time of one full call",
+        "note": "each step times one bounded sample on the host cores; ms_per_step is the "
+                "extrapolated time of one full call",
     }
     print(json.dumps(line), flush=True)
 
 
-def config_for(args, w: dict, world: int) -> dict:
-    bh = w["B"] * w["H"]
-    return {
-        "workload": args.workload,
-        "desc": w["desc"],
-        "batch": w["B"],
-        "heads": w["H"],
-        "seq_len": w["S"],
-        "head_dim": w["D"],
-        "scale_mode": "per_block128" if w["scale_mode"] == 1 else "per_bh",
-        "p_mode": "hilo" if args.p_mode == 1 else "e4m3",
-        "flops_per_call": flops_per_call(w),
-        "global_bh": bh * world if args.scaling == "weak" else bh,
-        "per_rank_bh": bh if args.scaling == "weak" else bh // world,
-        "parallelism": f"bh-shard x{world}",
-        "l2": "inputs (3 x %.2f GB bf16) exceed the 126 MB L2; no flush needed"
-        % (w["B"] * w["H"] * w["S"] * w["D"] * 2 / 1e9),
-    }
-
-
 # ---------------------------------------------------------------- B200 arm
+class Runner:
+    """Builds the per-rank inputs and one step of the hot path for a workload."""
+
+    def __init__(self, args, w: dict, rank: int, world: int, dev) -> None:  # type: ignore[no-untyped-def]
+        import torch
+
+        from repercep_runtime_b200 import ops
+
+        self.args, self.w, self.rank, self.world, self.dev = args, w, rank, world, dev
+        self.stream = torch.cuda.current_stream(dev)
+        self.mode = parallel_mode(args, w, world)
+        self.launches_per_step = 2
+        d = str(dev)
+        if w["kind"] == "decode":
+            from repercep_runtime_b200.attention import SharedPrefixFP8Decode
+
+            C, T, H, P, D = w["C"], w["T"], w["H"], w["P"], w["D"]
+            self.op = SharedPrefixFP8Decode(p_mode=args.p_mode)
+            self.q = gen_tensor((C * T, H, D), w["dist"], 100 * rank + 1, d)
+            self.kx = gen_tensor((C * T, H, D), w["dist"], 100 * rank + 2, d)
+            self.vx = gen_tensor((C * T, H, D), w["dist"], 100 * rank + 3, d)
+            kp = gen_tensor((P, H, D), w["dist"], 100 * rank + 4, d)
+            vp = gen_tensor((P, H, D), w["dist"], 100 * rank + 5, d)
+            self.prefix = self.op.quantize_prefix(kp, vp)
+            self.rank_flops = flops_per_call(w)
+            self.job_flops = self.rank_flops * world
+            self.inputs = [self.q, self.kx, self.vx]
+            return
+        B, H, S, D = w["B"], w["H"], w["S"], w["D"]
+        self.scale_mode = w["scale_mode"]
+        if self.mode == "cp":
+            from repercep_runtime_b200.parallel import ContextParallelAttention, nccl_all_gather
+
+            self.cp = ContextParallelAttention(S, rank, world, all_gather=nccl_all_gather(),
+                                               p_mode=args.p_mode)
+            shape = (B, H, self.cp.shard.rows, D)
+            self.scale_mode = ops.SCALE_PER_BLOCK128
+            self.job_flops = flops_per_call(w)
+            self.rank_flops = 4.0 * B * H * self.cp.shard.rows * S * D
+        elif self.mode == "shard" and args.scaling == "strong":
+            from repercep_runtime_b200.parallel import shard_bh
+
+            a, b = shard_bh(B, H, rank, world)
+            shape = (1, b - a, S, D)
+            self.job_flops = flops_per_call(w)
+            self.rank_flops = 4.0 * (b - a) * S * S * D
+        else:
+            shape = (B, H, S, D)
+            self.rank_flops = flops_per_call(w)
+            self.job_flops = self.rank_flops * world
+        self.launches_per_step = 1 + (2 if self.scale_mode == ops.SCALE_PER_BH else 1)
+        self.inputs = [gen_tensor(shape, w["dist"], 1000 * rank + i, d) for i in range(3)]
+
+    def step(self, ev=None):  # type: ignore[no-untyped-def]
+        """One pass of the hot path; `ev` brackets the dominant kernel."""
+        import torch
+
+        from repercep_runtime_b200 import ops
+
+        if self.w["kind"] == "decode":
+            qq, kx, vx = ops.quantize_fp8(
+                (self.q.unsqueeze(0), self.kx.unsqueeze(0), self.vx.unsqueeze(0)),
+                scale_mode=ops.SCALE_PER_BLOCK128, layout="bshd")
+            if ev:
+                ev[0].record(self.stream)
+            out = ops.prefix_decode_fp8_quantized(qq, self.prefix.k, self.prefix.v, kx, vx,
+                                                  candidates=self.w["C"], tokens=self.w["T"],
+                                                  p_mode=self.args.p_mode)
+            if ev:
+                ev[1].record(self.stream)
+            return out
+        q, k, v = self.inputs
+        qq, kq, vq = ops.quantize_fp8((q, k, v), scale_mode=self.scale_mode)
+        if self.mode == "cp":
+            B, H, rows, D = q.shape
+            k_all, v_all, ks_all, vs_all = self.cp.gather_kv(
+                kq.data.view(torch.uint8).reshape(B * H, rows, D),
+                vq.data.view(torch.uint8).reshape(B * H, rows, D), kq.scales, vq.scales)
+            if ev:
+                ev[0].record(self.stream)
+            out = ops.attention_fp8_chunked(qq, k_all.view(ops.FP8), v_all.view(ops.FP8), ks_all, vs_all,
+                                            last_rows=self.cp.shard.last_rows, p_mode=self.args.p_mode)
+        else:
+            if ev:
+                ev[0].record(self.stream)
+            out = ops.attention_fp8_quantized(qq, kq, vq, p_mode=self.args.p_mode)
+        if ev:
+            ev[1].record(self.stream)
+        return out
+
+    def quantized_suffix(self):  # type: ignore[no-untyped-def]
+        from repercep_runtime_b200 import ops
+
+        return ops.quantize_fp8((self.q.unsqueeze(0), self.kx.unsqueeze(0), self.vx.unsqueeze(0)),
+                                scale_mode=ops.SCALE_PER_BLOCK128, layout="bshd")
+
+    def decode_kernel(self, qq, kx, vx):  # type: ignore[no-untyped-def]
+        from repercep_runtime_b200 import ops
+
+        return ops.prefix_decode_fp8_quantized(qq, self.prefix.k, self.prefix.v, kx, vx,
+                                               candidates=self.w["C"], tokens=self.w["T"],
+                                               p_mode=self.args.p_mode)
+
+    def public_call(self, host_inputs, dev_inputs):  # type: ignore[no-untyped-def]
+        """The user-facing call on device copies of host inputs."""
+        if self.w["kind"] == "decode":
+            q, kx, vx = dev_inputs
+            return self.op(q, self.prefix, kx, vx, candidates=self.w["C"], tokens=self.w["T"])
+        if self.mode == "cp":
+            return self.cp(*dev_inputs)
+        from repercep_runtime_b200.attention import B200FP8Attention
+
+        if not hasattr(self, "_op"):
+            self._op = B200FP8Attention(scale_mode=self.scale_mode, p_mode=self.args.p_mode)
+        return self._op(*dev_inputs)
+
+
+def dominant_roofline(w: dict, runner: Runner, kernel_ms: float, peaks: dict) -> dict:
+    if w["kind"] == "decode":
+        C, T, H, P, D = w["C"], w["T"], w["H"], w["P"], w["D"]
+        rows = C * T
+        # e4m3 Q + prefix K/V + suffix K/V read once, bf16 output written once
+        algo = H * D * (rows + 2 * P + 2 * rows) + rows * H * D * 2
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        return {"bound": "hbm", "achieved": algo / (kernel_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                "frac": algo / (kernel_ms / 1e3) / 1e9 / peak, "traffic": profile_traffic("decode"),
+                "algorithmic_bytes": algo, "kernel": "fa8_fwd_kernel<1,%d> (prefix decode)" % runner.args.p_mode,
+                "peak_source": "of measured" if "hbm_gbs" in peaks else "of fallback"}
+    if "bf16_tflops_sustained" in peaks:
+        peak = 2.0 * float(peaks["bf16_tflops_sustained"])
+        src = "of measured: 2 x MEASURED_PEAKS bf16_tflops_sustained (B200 dense e4m3 rate = 2x bf16)"
+    else:
+        peak, src = 2.0 * 1400.0, "of fallback: 2 x 1.4 PFLOP/s sustained bf16"
+    ach = runner.rank_flops / (kernel_ms / 1e3) / 1e12
+    return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+            "traffic": profile_traffic(runner.args.workload), "peak_source": src,
+            "kernel": "fa8_fwd_kernel<2,%d>" % runner.args.p_mode}
+
+
 def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
 
-    from repercep_runtime_b200 import _lib, ops
-    from repercep_runtime_b200.attention import B200FP8Attention
+    from repercep_runtime_b200 import _lib
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    wl = dict(w)
-    if args.scaling == "strong" and world > 1:
-        # shard the B*H slices of one call: ranks take whole heads of both batches
-        if w["H"] % world:
-            raise SystemExit(f"H={w['H']} does not split over {world} ranks")
-        wl["H"] = w["H"] // world
-    q, k, v = gen_inputs(wl, seed=1000 * rank + 1, device=str(dev))
-    flops = flops_per_call(wl)
-    stream = torch.cuda.current_stream(dev)
+    runner = Runner(args, w, rank, world, dev)
+    stream = runner.stream
 
-    def step(ev_pair=None):
-        qq, kq, vq = ops.quantize_fp8((q, k, v), scale_mode=wl["scale_mode"])
-        if ev_pair is not None:
-            ev_pair[0].record(stream)
-        out = ops.attention_fp8_quantized(qq, kq, vq, p_mode=args.p_mode)
-        if ev_pair is not None:
-            ev_pair[1].record(stream)
-        return out
+    def barrier():  # type: ignore[no-untyped-def]
+        if world > 1:
+            dist.barrier()
 
     for _ in range(args.warmup):
-        step()
+        runner.step()
     torch.cuda.synchronize(dev)
     _lib.device_status(reset=True)
 
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
+    # Launch-bound workloads (decode: microseconds of GPU work per step) are
+    # captured once as CUDA graphs and replayed, so host submission latency
+    # is not timed as GPU time; the kernels and their arguments are the same.
+    graphs = None
+    if runner.w["kind"] == "decode" and not args.no_graph:
+        g_step, g_kernel = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step):
+            runner.step()
+        qq, kx, vx = runner.quantized_suffix()
+        with torch.cuda.graph(g_kernel):
+            runner.decode_kernel(qq, kx, vx)
+        for _ in range(args.warmup):
+            g_step.replay()
+            g_kernel.replay()
+        torch.cuda.synchronize(dev)
+        graphs = (g_step, g_kernel)
+
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank)
-    if world > 1:
-        dist.barrier()
+    barrier()
     torch.cuda.synchronize(dev)
     sampler.start()
-    time.sleep(0.3)  # let the sampler start before the timed region
+    time.sleep(0.3)  # the sampler's first reading lands inside the timed region
     t0.record(stream)
     for i in range(args.steps):
-        step(kev[i])
+        if graphs is None:
+            runner.step(kev[i])
+        else:
+            graphs[0].replay()
     t1.record(stream)
+    if graphs is not None:  # the dominant kernel alone, same graph mechanism
+        for i in range(args.steps):
+            kev[i][0].record(stream)
+            graphs[1].replay()
+            kev[i][1].record(stream)
     torch.cuda.synchronize(dev)
     clocks = sampler.stop()
-    if world > 1:
-        dist.barrier()
+    barrier()
     ms_total = t0.elapsed_time(t1)
-    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
     status = _lib.device_status()
-
-    t = torch.tensor([ms_total, attn_ms], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms_total, kernel_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total, attn_ms_max = float(t[0]), float(t[1])
+    ms_total, kernel_ms_max = float(t[0]), float(t[1])
     ms_step = ms_total / args.steps
-    value = flops * world * args.steps / (ms_total / 1e3) / 1e12
+    value = runner.job_flops * args.steps / (ms_total / 1e3) / 1e12
 
-    # e2e through the public AttentionOp with host buffers (pinned), copies timed
     e2e = None
     if not args.no_e2e:
-        op = B200FP8Attention(scale_mode=wl["scale_mode"], p_mode=args.p_mode)
-        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-        dq, dk, dv = (torch.empty_like(x) for x in (q, k, v))
-        hout = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
+        host = [x.cpu().pin_memory() for x in runner.inputs]
+        devc = [torch.empty_like(x) for x in runner.inputs]
+        out0 = runner.public_call(host, devc)
+        hout = torch.empty(out0.shape, dtype=out0.dtype, pin_memory=True)
 
-        def e2e_step():
-            dq.copy_(hq, non_blocking=True)
-            dk.copy_(hk, non_blocking=True)
-            dv.copy_(hv, non_blocking=True)
-            o = op(dq, dk, dv)
-            hout.copy_(o, non_blocking=True)
+        def e2e_step():  # type: ignore[no-untyped-def]
+            for dd, hh in zip(devc, host):
+                dd.copy_(hh, non_blocking=True)
+            hout.copy_(runner.public_call(host, devc), non_blocking=True)
 
         e2e_step()
         torch.cuda.synchronize(dev)
         n_e2e = max(1, min(args.steps, 5))
-        if world > 1:
-            dist.barrier()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         for _ in range(n_e2e):
             e2e_step()
@@ -375,66 +535,43 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = float(te[0]) / n_e2e
-        nbytes = q.numel() * 2
         e2e = {
-            "value": flops * world / (e2e_ms / 1e3) / 1e12,
+            "value": runner.job_flops / (e2e_ms / 1e3) / 1e12,
             "unit": UNIT,
-            "h2d_bytes_per_step": 3 * nbytes,
-            "d2h_bytes_per_step": nbytes,
+            "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in host),
+            "d2h_bytes_per_step": hout.numel() * hout.element_size(),
             "ms_per_step": e2e_ms,
-            "api": "B200FP8Attention.__call__ (AttentionOp) with pinned host Q/K/V in, host O out",
+            "api": "public op __call__ (B200FP8Attention / SharedPrefixFP8Decode / "
+                   "ContextParallelAttention) on pinned host inputs, output copied back",
         }
-        del hq, hk, hv, dq, dk, dv, hout
 
     if rank != 0:
         return
     peaks = load_peaks()
-    if "bf16_tflops_sustained" in peaks:
-        peak = 2.0 * float(peaks["bf16_tflops_sustained"])
-        peak_src = "of measured: 2 x MEASURED_PEAKS bf16_tflops_sustained (B200 dense e4m3 rate = 2x bf16)"
-    else:
-        peak = 2.0 * 1400.0
-        peak_src = "of fallback: 2 x 1.4 PFLOP/s sustained bf16"
-    attn_tflops = flops / (attn_ms / 1e3) / 1e12
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         r = cpu_reference_sample(w)
         cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
-    traffic = profile_traffic(args.workload)
+    per_gpu = value / world
     line = {
-        "metric": METRIC,
-        "value": value,
-        "unit": UNIT,
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms_step,
-        "higher_is_better": True,
-        "scaling": args.scaling,
-        "vs_baseline": None,
-        "dtype": "fp8_e4m3",
-        "data": "synthetic",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong" if (runner.mode == "cp" or (runner.mode == "shard" and args.scaling == "strong"))
+        else "weak",
+        "vs_baseline": None, "dtype": "fp8_e4m3", "data": "synthetic",
         "config": config_for(args, w, world),
-        "tflops_per_gpu": value / world,
-        "pct_fp8_peak_nominal": 100.0 * value / world / FP8_NOMINAL_TFLOPS,
-        "pct_fp8_peak_measured": 100.0 * value / world / peak,
+        "tflops_per_gpu": per_gpu,
+        "pct_fp8_peak_nominal": 100.0 * per_gpu / FP8_NOMINAL_TFLOPS,
+        "pct_fp8_peak_measured": 100.0 * per_gpu / (2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))),
         "ms_per_call": ms_step,
-        "attn_kernel_ms": attn_ms,
-        "attn_kernel_ms_max_rank": attn_ms_max,
-        "roofline": {
-            "bound": "tensor",
-            "achieved": attn_tflops,
-            "peak": peak,
-            "unit": "TFLOP/s",
-            "frac": attn_tflops / peak,
-            "traffic": traffic,
-            "peak_source": peak_src,
-            "kernel": "fa8_fwd_kernel<2,%d>" % args.p_mode,
-        },
+        "kernel_ms": kernel_ms,
+        "kernel_ms_max_rank": kernel_ms_max,
+        "roofline": dominant_roofline(w, runner, kernel_ms, peaks),
         "cpu_baseline": cpu,
         "e2e": e2e,
         "clocks": clocks,
-        "gpu_launches": args.steps * (2 if wl["scale_mode"] == 0 else 1) + args.steps,
+        "gpu_launches": args.steps * runner.launches_per_step,
+        "cuda_graph": graphs is not None,
         "device_status": status,
     }
     print(json.dumps(line), flush=True)
@@ -451,6 +588,7 @@ def main() -> None:
     ap.add_argument("--p-mode", type=int, choices=(0, 1), default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="decode: launch eagerly instead of replaying a CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -463,6 +601,8 @@ def main() -> None:
     if args.impl == "reference":
         run_reference_arm(args, w, rank, world)
         return
+    if w["kind"] == "cpu":
+        ap.error(f"workload {args.workload!r} is the reference's CPU case; use --impl reference")
 
     import datetime
 
@@ -471,11 +611,8 @@ def main() -> None:
 
     if world > 1:
         torch.cuda.set_device(local_rank)
-        dist.init_process_group(
-            "nccl",
-            timeout=datetime.timedelta(seconds=120),
-            device_id=torch.device("cuda", local_rank),
-        )
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
     try:
         run_b200_arm(args, w, rank, world, local_rank)
     finally:
