@@ -41,25 +41,32 @@ constexpr int kTileBytes = kTile * kTile;
 constexpr int kKSt = 3;
 constexpr int kVSt = 3;
 constexpr int kDefaultExpPoly = 2;
-constexpr int kDefaultPingPong = 0;
+constexpr int kDefaultRowSplit = 1;
 
 // Pipeline tracing (compiled in only with -DRP_PIPELINE_TRACE): one chosen CTA
 // records (SM clock, event << 16 | step) at every barrier hand-off of every
 // role, for offline timeline analysis.  The product build has none of it.
 #ifdef RP_PIPELINE_TRACE
-// Slot (event, step) of the traced CTA; plain stores, so recording does not
-// stall the recording thread.
+// Slot (event, step) of the traced CTA; each role reads the target once
+// (RP_TRACE_INIT) so recording is a clock read and a plain store.
 __device__ uint32_t* g_trace_buf = nullptr;
 __device__ int g_trace_x = -1;
 __device__ int g_trace_y = -1;
 constexpr int kTraceSteps = 1024;  // events < 256
-__device__ __forceinline__ void trace_event(int ev, int j) {
-  if (g_trace_buf == nullptr || (int)blockIdx.x != g_trace_x || (int)blockIdx.y != g_trace_y)
-    return;
-  g_trace_buf[ev * kTraceSteps + (j & (kTraceSteps - 1))] = static_cast<uint32_t>(clock64());
+__device__ __forceinline__ uint32_t* trace_target() {
+  return (g_trace_buf != nullptr && (int)blockIdx.x == g_trace_x && (int)blockIdx.y == g_trace_y)
+             ? g_trace_buf
+             : nullptr;
 }
-#define RP_TRACE(ev, j) trace_event((ev), (j))
+#define RP_TRACE_INIT() uint32_t* const rp_trace_buf_ = trace_target()
+#define RP_TRACE(ev, j)                                                                   \
+  do {                                                                                    \
+    if (rp_trace_buf_)                                                                    \
+      rp_trace_buf_[(ev) * kTraceSteps + ((j) & (kTraceSteps - 1))] =                     \
+          static_cast<uint32_t>(clock64());                                               \
+  } while (0)
 #else
+#define RP_TRACE_INIT() ((void)0)
 #define RP_TRACE(ev, j) ((void)0)
 #endif
 
@@ -75,12 +82,14 @@ enum : int {
   kErrWaitO = 0x109,
   kErrWaitEpi = 0x10A,
   kErrWaitOFinal = 0x10B,
-  kErrWaitTok = 0x10C,
+  kErrWaitX = 0x10C,
 };
 
-template <int NQ, int PMODE>
+template <int NQ, int PMODE, int NSPLIT = 1>
 struct Cfg {
-  static constexpr int kSoftmaxWarps = 4 * NQ;
+  static constexpr int kNC = kTile / NSPLIT;                 // S columns per softmax thread
+  static constexpr int kWarpsPerTile = 4 * NSPLIT;
+  static constexpr int kSoftmaxWarps = kWarpsPerTile * NQ;
   static constexpr int kTmaWarp = kSoftmaxWarps;
   static constexpr int kMmaWarp = kSoftmaxWarps + 1;
   static constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
@@ -92,15 +101,17 @@ struct Cfg {
   static constexpr int kOffV = kOffK + kKSt * kTileBytes;
   static constexpr int kOffP = kOffV + kVSt * kTileBytes;
   static constexpr int kPStride = kPParts * kTileBytes;
-  static constexpr int kOffBar = kOffP + NQ * kPBuf * kPStride;
-  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 8;
+  static constexpr int kOffX = kOffP + NQ * kPBuf * kPStride;  // row-max / row-sum exchange
+  static constexpr int kXBytes = (NSPLIT == 2) ? NQ * 3 * 2 * kTile * 4 : 0;
+  static constexpr int kOffBar = kOffX + kXBytes;
+  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Bars {
   uint64_t *q_full, *k_full, *k_empty, *v_full, *v_empty;
-  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *tok;
+  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *xch;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -121,8 +132,8 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   b.o_final = b.o_done + NQ;
   b.epi = b.o_final + NQ;
   b.fin = b.epi + NQ;
-  b.tok = b.fin + 1;  // [2][4]: exp-phase hand-over between paired warps
-  b.tmem_slot = reinterpret_cast<uint32_t*>(b.tok + 8);
+  b.xch = b.fin + 1;  // [NQ][4 lane quarters][3]: row-max (x2 by step parity), row-sum
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.xch + 12 * NQ);
   b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
   return b;
 }
@@ -221,6 +232,7 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
                          const CUtensorMap* tm_kx, const CUtensorMap* tm_vx,
                          const AttnKernelParams& p, const Bars& bar, uint8_t* smem, int n_steps) {
   using C = Cfg<NQ, PMODE>;
+  RP_TRACE_INIT();
   const int bh = blockIdx.y;
   const int qt0 = blockIdx.x * NQ;
   mbar_arrive_expect_tx(bar.q_full, NQ * kTileBytes);
@@ -276,6 +288,7 @@ template <int NQ, int PMODE>
 __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& bar,
                                          uint32_t sbase, uint32_t tmem, int i, bool last) {
   using C = Cfg<NQ, PMODE>;
+  RP_TRACE_INIT();
   constexpr uint32_t idesc_pv = make_idesc_e4m3(128, 128, 0, 1);
   const int vsl = i % kVSt;
   if (!mbar_wait(bar.v_full + vsl, (i / kVSt) & 1, bar.abort_flag, p.status, kErrWaitV))
@@ -316,6 +329,7 @@ template <int NQ, int PMODE>
 __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* smem,
                            uint32_t tmem, int n_steps) {
   using C = Cfg<NQ, PMODE>;
+  RP_TRACE_INIT();
   constexpr uint32_t idesc_qk = make_idesc_e4m3(128, 128, 0, 0);
   const uint32_t sbase = smem_u32(smem);
   bool ok = mbar_wait(bar.q_full, 0, bar.abort_flag, p.status, kErrWaitQ);
@@ -353,20 +367,33 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
 }
 
 // ----------------------------------------------------------------- softmax
-template <int NQ, int PMODE, int EPOLY, int PP>
+// NSPLIT threads share each query row: thread (half, row) owns S columns
+// [half * kNC, half * kNC + kNC).  With NSPLIT = 2 the two halves swap their
+// partial row maxima through shared memory every step and their partial row
+// sums once at the end.
+template <int NQ, int PMODE, int EPOLY, int NSPLIT>
 __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
                            uint8_t* smem, uint32_t tmem, int n_steps) {
-  using C = Cfg<NQ, PMODE>;
+  using C = Cfg<NQ, PMODE, NSPLIT>;
+  RP_TRACE_INIT();
+  constexpr int NC = C::kNC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = warp >> 2, wq = warp & 3;
+  const int t = warp / C::kWarpsPerTile;
+  const int sub = warp % C::kWarpsPerTile;
+  const int half = sub >> 2, wq = sub & 3;
   const int row = wq * 32 + lane;
+  const int col0 = half * NC;
+  const bool tracer = (wq == 0 && lane == 0 && half == 0);
   const int bh = blockIdx.y;
   const int q_tile = blockIdx.x * NQ + t;
   const int q_tile_c = min(q_tile, p.n_q_tiles - 1);
   const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-  const uint32_t tS = tmem + lane_base + t * kTile;
-  const uint32_t tO = tmem + lane_base + (NQ + t) * kTile;
+  const uint32_t tS = tmem + lane_base + t * kTile + col0;
+  const uint32_t tO = tmem + lane_base + (NQ + t) * kTile + col0;
   uint8_t* pbase = smem + C::kOffP + t * C::kPBuf * C::kPStride;
+  // exchange slots: [t][parity 0,1 = row max, 2 = row sum][half][row]
+  float* xch = reinterpret_cast<float*>(smem + C::kOffX) + t * 3 * 2 * kTile;
+  uint64_t* xbar = bar.xch + (t * 4 + wq) * 3;
 
   const float sq = p.qs[bh * p.qs_bh + q_tile_c * p.qs_blk];
 
@@ -382,7 +409,6 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     vbits = max(vbits, __float_as_uint(p.vsx[bh * p.kvx_bh + q_tile_c * p.kvx_blk]));
   vbits = __reduce_max_sync(0xffffffffu, vbits);
   const float sv_max = __uint_as_float(vbits);
-
   const float inv_svmax = 1.f / sv_max;
 
   // Per-step constants: c_j (log2-domain score scale), log2 K_j and 1/K_j
@@ -424,88 +450,88 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     int c, tt, valid;
     bool extra;
     step_info(p, j, c, tt, valid, extra);
-    if (wq == 0 && lane == 0) RP_TRACE(100 + t, j);
+    if (tracer) RP_TRACE(100 + t, j);
 
     if (!warp_wait(bar.s_full + t, j & 1, bar.abort_flag, p.status, kErrWaitS)) {
       ok = false;
       break;
     }
-    if (wq == 0 && lane == 0) RP_TRACE(10 + t, j);
+    if (tracer) RP_TRACE(10 + t, j);
     tc_fence_after();
-    uint32_t r[4][32];
+    uint32_t r[NC / 32][32];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, r[q]);
+    for (int q = 0; q < NC / 32; ++q) tmem_ld32(tS + 32 * q, r[q]);
     tmem_wait_ld();
-    if (wq == 0 && lane == 0) RP_TRACE(104 + t, j);
+    if (tracer) RP_TRACE(104 + t, j);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(bar.s_free + t);
 
-    float s[128];
+    float s[NC];
 #pragma unroll
-    for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(r[i >> 5][i & 31]);
+    for (int i = 0; i < NC; ++i) s[i] = __uint_as_float(r[i >> 5][i & 31]);
 
     if (!extra && valid < kTile) {
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
-        if (i >= valid) s[i] = -INFINITY;
+      for (int i = 0; i < NC; ++i)
+        if (col0 + i >= valid) s[i] = -INFINITY;
     }
     if (p.causal) {
       const int rel = (q_tile * kTile + row) - tt * kTile;  // column i allowed iff i <= rel
       if (rel < kTile - 1) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i > rel) s[i] = -INFINITY;
+        for (int i = 0; i < NC; ++i)
+          if (col0 + i > rel) s[i] = -INFINITY;
       }
     }
     if (extra) {
       const int g0 = (row / p.extra_group) * p.extra_group;  // own candidate's first token
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
-        if (i < g0 || i > row) s[i] = -INFINITY;
+      for (int i = 0; i < NC; ++i)
+        if (col0 + i < g0 || col0 + i > row) s[i] = -INFINITY;
     }
 
-    // Row max: eight independent chains of 3-input max, then a short tree.
-    float a8[8];
+    // Row max: independent chains of 3-input max (16 columns each), a short tree.
+    constexpr int NCH = NC / 16;
+    float ach[NCH];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < NCH; ++k) {
       float acc = s[16 * k];
 #pragma unroll
       for (int jj = 0; jj < 7; ++jj) acc = fmax3f(acc, s[16 * k + 1 + 2 * jj], s[16 * k + 2 + 2 * jj]);
-      a8[k] = fmaxf(acc, s[16 * k + 15]);
+      ach[k] = fmaxf(acc, s[16 * k + 15]);
     }
-    const float mx =
-        fmax3f(fmax3f(a8[0], a8[1], a8[2]), fmax3f(a8[3], a8[4], a8[5]), fmaxf(a8[6], a8[7]));
-    if (wq == 0 && lane == 0) RP_TRACE(106 + t, j);
+    float mx = ach[0];
+#pragma unroll
+    for (int k = 1; k < NCH; ++k) mx = fmaxf(mx, ach[k]);
+    if constexpr (NSPLIT == 2) {
+      // swap partial maxima with the warp that owns the other half of these rows
+      xch[((j & 1) * 2 + half) * kTile + row] = mx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xbar + (j & 1));
+      if (!warp_wait(xbar + (j & 1), (j >> 1) & 1, bar.abort_flag, p.status, kErrWaitX)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, xch[((j & 1) * 2 + (1 - half)) * kTile + row]);
+    }
+    if (tracer) RP_TRACE(106 + t, j);
     const float m_new = fmaxf(m_run, mx * cj);
     const bool grew = m_new > m_run;
     const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
     const float alpha = ex2_approx(m_run - m_use);
     const float noff = log2k - m_use;
 
-    // With PP (two query tiles), the exp phases of the two warps that share an
-    // SM sub-partition alternate: warpgroup 0's step j after warpgroup 1's
-    // step j-1, warpgroup 1's step j after warpgroup 0's step j.  While one
-    // warp streams its exps through MUFU the other does the rest of its step.
-    if constexpr (PP && NQ == 2) {
-      const bool need = (t == 1) || (j > 0);
-      const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
-      if (need && !warp_wait(bar.tok + 4 * t + wq, par, bar.abort_flag, p.status, kErrWaitTok)) {
-        ok = false;
-        break;
-      }
-    }
-
     // p' = 2^(s * c_j - m + log2 K_j).  Packed f32x2 FMAs form the exponents;
     // EPOLY of every 8 go through the FMA-pipe polynomial, the rest through
     // MUFU ex2; the row sum runs on four packed accumulators.
-    uint32_t pk[32];
-    uint32_t pl[(PMODE == 1) ? 32 : 1];
+    uint32_t pk[NC / 4];
+    uint32_t pl[(PMODE == 1) ? NC / 4 : 1];
     const uint64_t c2 = pack_f32x2(cj, cj);
     const uint64_t o2 = pack_f32x2(noff, noff);
     uint64_t sacc[4];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < NC / 8; ++i) {
       float x[8], e[8];
 #pragma unroll
       for (int h = 0; h < 4; ++h)
@@ -525,11 +551,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         pl[2 * i + 1] = pack_e4m3x4_residual(pk[2 * i + 1], e[4], e[5], e[6], e[7]);
       }
     }
-    if (wq == 0 && lane == 0) RP_TRACE(108 + t, j);
-    if constexpr (PP && NQ == 2) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar.tok + 4 * (1 - t) + wq);
-    }
+    if (tracer) RP_TRACE(108 + t, j);
     // Next step's constants (their MUFU ops queue behind this step's exps and
     // are consumed a whole step later), then the scale loads for step j+2.
     float cj_n = cj, log2k_n = log2k, invk_n = invk;
@@ -550,18 +572,23 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     }
     uint8_t* pb = pbase + ((C::kPBuf == 2) ? (j & 1) : 0) * C::kPStride;
     const uint32_t prow = smem_u32(pb) + row * 128;
+    constexpr int kChunks = NC / 16;  // 16-byte P chunks of this thread
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      st_shared_v4(prow + ((k ^ (row & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
+    for (int k = 0; k < kChunks; ++k) {
+      const int kg = half * kChunks + k;
+      st_shared_v4(prow + ((kg ^ (row & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
                    pk[4 * k + 3]);
+    }
     if constexpr (PMODE == 1) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        st_shared_v4(prow + kTileBytes + ((k ^ (row & 7)) << 4), pl[4 * k], pl[4 * k + 1],
+      for (int k = 0; k < kChunks; ++k) {
+        const int kg = half * kChunks + k;
+        st_shared_v4(prow + kTileBytes + ((kg ^ (row & 7)) << 4), pl[4 * k], pl[4 * k + 1],
                      pl[4 * k + 2], pl[4 * k + 3]);
+      }
     }
     fence_proxy_async_smem();
-    if (wq == 0 && lane == 0) RP_TRACE(20 + t, j);
+    if (tracer) RP_TRACE(20 + t, j);
 
     // O needs rescaling only when a row's running max grew; only then must
     // PV(j-1) have finished before O is touched.  (P buffer j&1 is already
@@ -572,32 +599,29 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         ok = false;
         break;
       }
-      if (wq == 0 && lane == 0) RP_TRACE(30 + t, j);
+      if (tracer) RP_TRACE(30 + t, j);
       tc_fence_after();
-      {
-        if (wq == 0 && lane == 0) RP_TRACE(90 + t, j);
+      const uint64_t a2 = pack_f32x2(alpha, alpha);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * q, o);
-          tmem_wait_ld();
-          const uint64_t a2 = pack_f32x2(alpha, alpha);
+      for (int q = 0; q < NC / 32; ++q) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * q, o);
+        tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float u0, u1;
-            unpack_f32x2(fmul2(pack_f32x2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), a2), u0, u1);
-            o[i] = __float_as_uint(u0);
-            o[i + 1] = __float_as_uint(u1);
-          }
-          tmem_st32(tO + 32 * q, o);
+        for (int i = 0; i < 32; i += 2) {
+          float u0, u1;
+          unpack_f32x2(fmul2(pack_f32x2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), a2), u0, u1);
+          o[i] = __float_as_uint(u0);
+          o[i + 1] = __float_as_uint(u1);
         }
-        tmem_wait_st();
+        tmem_st32(tO + 32 * q, o);
       }
+      tmem_wait_st();
     }
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(bar.p_full + 2 * t + (j & 1));
-    if (wq == 0 && lane == 0) RP_TRACE(40 + t, j);
+    if (tracer) RP_TRACE(40 + t, j);
     l_run = l_run * alpha + sum * invk;
     m_run = m_new;
     cj = cj_n;
@@ -609,6 +633,13 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   // unambiguous even though o_done phases were skipped above).
   if (ok && n_steps > 0)
     ok = warp_wait(bar.o_final + t, 0, bar.abort_flag, p.status, kErrWaitOFinal);
+  if (ok && NSPLIT == 2) {  // the two halves' row sums
+    xch[(2 * 2 + half) * kTile + row] = l_run;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xbar + 2);
+    ok = warp_wait(xbar + 2, 0, bar.abort_flag, p.status, kErrWaitX);
+    if (ok) l_run += xch[(2 * 2 + (1 - half)) * kTile + row];
+  }
   if (!ok) return;
 
   // Epilogue: O * (sv_max / 448) / l -> bf16, staged as two 128x64 halves in
@@ -617,12 +648,13 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   const float f = (sv_max / 448.f) / l_run;
   uint8_t* stage[2] = {smem + C::kOffQ + t * kTileBytes, pbase};
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
+  for (int hh = 0; hh < 2 / NSPLIT; ++hh) {
+    const int h = (NSPLIT == 2) ? half : hh;  // 64-column box this thread fills
     const uint32_t srow = smem_u32(stage[h]) + row * 128;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       uint32_t o[32];
-      tmem_ld32(tO + 64 * h + 32 * cc, o);
+      tmem_ld32(tO + 64 * hh + 32 * cc, o);
       tmem_wait_ld();
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -637,7 +669,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) mbar_arrive(bar.epi + t);
-  if (wq == 0 && lane == 0 && q_tile < p.n_q_tiles) {
+  if (wq == 0 && lane == 0 && half == 0 && q_tile < p.n_q_tiles) {
     if (mbar_wait(bar.epi + t, 0, bar.abort_flag, p.status, kErrWaitEpi)) {
       const int b = bh / p.H, h = bh % p.H;
       tma_store_4d(tm_o, stage[0], 0, q_tile * kTile, h, b);
@@ -648,14 +680,14 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int PP>
-__global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
+template <int NQ, int PMODE, int EPOLY, int NSPLIT>
+__global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    const __grid_constant__ CUtensorMap tm_kx,
                    const __grid_constant__ CUtensorMap tm_vx,
                    const __grid_constant__ CUtensorMap tm_o, const AttnKernelParams p) {
-  using C = Cfg<NQ, PMODE>;
+  using C = Cfg<NQ, PMODE, NSPLIT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -674,15 +706,15 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
     }
     for (int t = 0; t < NQ; ++t) {
       mbar_init(bar.s_full + t, 1);
-      mbar_init(bar.s_free + t, 4);
-      mbar_init(bar.p_full + 2 * t, 4);
-      mbar_init(bar.p_full + 2 * t + 1, 4);
+      mbar_init(bar.s_free + t, C::kWarpsPerTile);
+      mbar_init(bar.p_full + 2 * t, C::kWarpsPerTile);
+      mbar_init(bar.p_full + 2 * t + 1, C::kWarpsPerTile);
       mbar_init(bar.o_done + t, 1);
       mbar_init(bar.o_final + t, 1);
-      mbar_init(bar.epi + t, 4);
+      mbar_init(bar.epi + t, C::kWarpsPerTile);
     }
     mbar_init(bar.fin, 1);
-    for (int i = 0; i < 8; ++i) mbar_init(bar.tok + i, 1);
+    for (int i = 0; i < 12 * NQ; ++i) mbar_init(bar.xch + i, 2);
     *bar.abort_flag = 0;
     fence_barrier_init();
   }
@@ -712,7 +744,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
   } else if (warp == C::kMmaWarp) {
     if (lane == 0) mma_issuer<NQ, PMODE>(p, bar, smem, tmem, n_steps);
   } else {
-    softmax_wg<NQ, PMODE, EPOLY, PP>(&tm_o, p, bar, smem, tmem, n_steps);
+    softmax_wg<NQ, PMODE, EPOLY, NSPLIT>(&tm_o, p, bar, smem, tmem, n_steps);
   }
 
   tc_fence_before();
@@ -723,11 +755,11 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE>::kThreads, 1)
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int PP>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT>
 cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
                            cudaStream_t st) {
-  using C = Cfg<NQ, PMODE>;
-  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, PP>;
+  using C = Cfg<NQ, PMODE, NSPLIT>;
+  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, NSPLIT>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -756,13 +788,13 @@ int exp_poly_setting() {
   return v;
 }
 
-// Alternate the exp phases of the two softmax warpgroups (1) or let them
-// run freely (0).  REPERCEP_B200_PINGPONG overrides the default (read once).
-int pingpong_setting() {
+// Threads per query row in the softmax warpgroups (1 or 2).
+// REPERCEP_B200_ROW_SPLIT overrides the default (read once).
+int split_setting() {
   static const int v = [] {
-    const char* e = std::getenv("REPERCEP_B200_PINGPONG");
-    if (!e) return kDefaultPingPong;
-    return std::atoi(e) ? 1 : 0;
+    const char* e = std::getenv("REPERCEP_B200_ROW_SPLIT");
+    if (!e) return kDefaultRowSplit;
+    return std::atoi(e) == 2 ? 2 : 1;
   }();
   return v;
 }
@@ -782,20 +814,20 @@ extern "C" int rp_trace_setup(void* buf, int cta_x, int cta_y) {
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
                              int nq, int p_mode, cudaStream_t st) {
   const int ep = exp_poly_setting();
-  const int pp = pingpong_setting();
+  const int sp = split_setting();
   if (nq == 2 && p_mode == 0) {
-    if (pp) {
-      if (ep == 2) return launch_variant<2, 0, 2, 1>(maps, p, B, H, st);
-      if (ep == 4) return launch_variant<2, 0, 4, 1>(maps, p, B, H, st);
-      return launch_variant<2, 0, 0, 1>(maps, p, B, H, st);
+    if (sp == 2) {
+      if (ep == 0) return launch_variant<2, 0, 0, 2>(maps, p, B, H, st);
+      if (ep == 4) return launch_variant<2, 0, 4, 2>(maps, p, B, H, st);
+      return launch_variant<2, 0, 2, 2>(maps, p, B, H, st);
     }
-    if (ep == 2) return launch_variant<2, 0, 2, 0>(maps, p, B, H, st);
-    if (ep == 4) return launch_variant<2, 0, 4, 0>(maps, p, B, H, st);
-    return launch_variant<2, 0, 0, 0>(maps, p, B, H, st);
+    if (ep == 0) return launch_variant<2, 0, 0, 1>(maps, p, B, H, st);
+    if (ep == 4) return launch_variant<2, 0, 4, 1>(maps, p, B, H, st);
+    return launch_variant<2, 0, 2, 1>(maps, p, B, H, st);
   }
-  if (nq == 2 && p_mode == 1) return launch_variant<2, 1, 0, 0>(maps, p, B, H, st);
-  if (nq == 1 && p_mode == 0) return launch_variant<1, 0, 0, 0>(maps, p, B, H, st);
-  if (nq == 1 && p_mode == 1) return launch_variant<1, 1, 0, 0>(maps, p, B, H, st);
+  if (nq == 2 && p_mode == 1) return launch_variant<2, 1, 0, 1>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 0) return launch_variant<1, 0, 2, 1>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 1) return launch_variant<1, 1, 0, 1>(maps, p, B, H, st);
   return cudaErrorInvalidValue;
 }
 
