@@ -70,6 +70,13 @@ const char* rp_last_error(void);
  * when `reset` is non-zero it is cleared afterwards.  Diagnostic only. */
 int rp_device_status(int* status, int reset);
 
+/* Online-softmax rescale threshold (log2 units) the attention kernels use:
+ * O and the row sums are rescaled only when a row max grows by more than
+ * this, and P is rounded at 2^-tau of its usual scale meanwhile (0 = rescale
+ * on every growth, as the reference kernel does).  Set once per process by
+ * REPERCEP_B200_RESCALE_TAU (0..8); default 1.  No reference counterpart. */
+float rp_attn_rescale_tau(void);
+
 /* Workspace bytes rp_quant_fp8_e4m3 needs (0 for RP_SCALE_PER_BLOCK128). */
 int rp_quant_workspace_bytes(int num_tensors, int B, int H, int S, int D, int scale_mode,
                              size_t* bytes);

@@ -102,8 +102,16 @@ def reference_tile_loop(
     causal: bool = False,
     block_n: int = 128,
     fp8_max: float = 448.0,
+    rescale_tau: float = 0.0,
 ) -> np.ndarray:
-    """The reference kernel's FA-2 loop in fp32; returns (BH, Sq, D) fp32."""
+    """The reference kernel's FA-2 loop in fp32; returns (BH, Sq, D) fp32.
+
+    ``rescale_tau`` = 0 is the reference loop.  A positive value models the
+    B200 kernel's rescale threshold (log2 units): within each group of 32
+    query rows the running max is raised only when some row's max would grow
+    by more than ``rescale_tau``; meanwhile p may reach 2^tau, so P is rounded
+    as e4m3(p * fp8_max * 2^-tau) and the PV product is scaled back by 2^tau.
+    """
     BH, Sq, D = q8.shape
     Skv = k8.shape[1]
     out = np.empty((BH, Sq, D), dtype=np.float32)
@@ -126,14 +134,23 @@ def reference_tile_loop(
             if causal:
                 qk = np.where(rows >= cols, qk, -np.inf)
             qk = np.where(cols < Skv, qk, -np.inf).astype(np.float32)
-            m_new = np.maximum(m, qk.max(axis=1))
-            with np.errstate(invalid="ignore"):
-                alpha = np.exp(m - m_new).astype(np.float32)
-            p = np.exp(qk - m_new[:, None]).astype(np.float32)
+            m_cand = np.maximum(m, qk.max(axis=1))
+            if rescale_tau > 0:
+                with np.errstate(invalid="ignore"):
+                    need = m_cand > m + np.float32(rescale_tau * np.log(2.0))
+                need = np.concatenate([need, np.zeros((-Sq) % 32, dtype=bool)])
+                grp = np.repeat(need.reshape(-1, 32).any(axis=1), 32)[:Sq]
+                m_new = np.where(grp, m_cand, m).astype(np.float32)
+            else:
+                m_new = m_cand
+            m_use = np.where(m_new == -np.inf, np.float32(0), m_new).astype(np.float32)
+            alpha = np.exp(m - m_use).astype(np.float32)
+            p = np.exp(qk - m_use[:, None]).astype(np.float32)
             l = l * alpha + p.sum(axis=1, dtype=np.float32)
             acc = acc * alpha[:, None]
-            p8 = e4m3_decode(e4m3_encode((p * np.float32(fp8_max)).astype(np.float32)))
-            acc = acc + (p8 @ vt).astype(np.float32) * pv_scale
+            shift = np.float32(2.0**-rescale_tau)
+            p8 = e4m3_decode(e4m3_encode((p * np.float32(fp8_max) * shift).astype(np.float32)))
+            acc = acc + (p8 @ vt).astype(np.float32) * (pv_scale / shift)
             m = m_new
         out[bh] = acc / l[:, None]
     return out

@@ -39,6 +39,7 @@ _c_i64_p = ctypes.POINTER(ctypes.c_int64)
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rp_abi_version": (_c_int, []),
     "rp_last_error": (ctypes.c_char_p, []),
+    "rp_attn_rescale_tau": (_c_float, []),
     "rp_device_status": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
     "rp_quant_workspace_bytes": (
         _c_int,
@@ -152,6 +153,11 @@ def i64_array(values) -> ctypes.Array:  # type: ignore[type-arg]
 def ptr_array(values) -> ctypes.Array:  # type: ignore[type-arg]
     vals = [int(v) for v in values]
     return (_c_void_p * len(vals))(*vals)
+
+
+def rescale_tau() -> float:
+    """Online-softmax rescale threshold (log2 units) of the attention kernels."""
+    return float(load().rp_attn_rescale_tau())
 
 
 def device_status(reset: bool = False) -> int:

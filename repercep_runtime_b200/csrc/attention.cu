@@ -42,6 +42,7 @@ constexpr int kKSt = 3;
 constexpr int kVSt = 3;
 constexpr int kDefaultExpPoly = 2;
 constexpr int kDefaultRowSplit = 1;
+constexpr float kDefaultRescaleTau = 1.0f;
 
 // Pipeline tracing (compiled in only with -DRP_PIPELINE_TRACE): one chosen CTA
 // records (SM clock, event << 16 | step) at every barrier hand-off of every
@@ -226,6 +227,31 @@ __device__ __forceinline__ void step_info(const AttnKernelParams& p, int j, int&
   valid = min(kTile, len - t * kTile);
 }
 
+// The same (chunk, tile) walk as step_info, one step at a time without a
+// division (main tiles only; the extra tile is handled by the caller).
+struct StepCursor {
+  int c = 0, t = 0;
+  __device__ __forceinline__ void next(const AttnKernelParams& p) {
+    if (++t == p.tiles_per_chunk) {
+      t = 0;
+      ++c;
+    }
+  }
+  __device__ __forceinline__ int valid(const AttnKernelParams& p) const {
+    const int len = (c == p.n_chunks - 1) ? p.last_len : p.chunk_len;
+    return min(kTile, len - t * kTile);
+  }
+};
+
+// Orders every later use of `r` after the preceding tcgen05.wait::ld: the
+// compiler sees the registers redefined here, after the (volatile) wait.
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8)
+    asm volatile("" : "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]),
+                 "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7]));
+}
+
 // ------------------------------------------------------------ TMA producer
 template <int NQ, int PMODE>
 __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
@@ -242,10 +268,11 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
 
   int nk = 0, nv = 0;
   bool ok = true;
+  StepCursor cur;
   for (int j = 0; j < n_steps && ok; ++j) {
-    int c, t, valid;
-    bool extra;
-    step_info(p, j, c, t, valid, extra);
+    const bool extra = p.has_extra && j == p.n_main_tiles;
+    const int c = cur.c, t = cur.t;
+    if (!extra) cur.next(p);
     const int ks = j % kKSt, ku = j / kKSt;
     if (ku > 0 && !mbar_wait(bar.k_empty + ks, (ku - 1) & 1, bar.abort_flag, p.status,
                              kErrWaitKEmpty)) {
@@ -415,18 +442,17 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   // (K_j = 448 * sv_j / sv_max, the P scale).  They are formed one step
   // ahead, after the exp loop, and their scale loads two steps ahead, so no
   // global load, division or MUFU op sits on the path between two steps.
+  StepCursor ahead;  // K/V tile of the next scale load
   auto load_step = [&](int j, float& sk, float& sv) {
-    int c, tt, valid;
-    bool extra;
-    step_info(p, j, c, tt, valid, extra);
-    if (extra) {
+    if (p.has_extra && j == p.n_main_tiles) {
       const int idx = bh * p.kvx_bh + q_tile_c * p.kvx_blk;
       sk = p.ksx[idx];
       sv = p.vsx[idx];
     } else {
-      const int64_t idx = c * p.kv_chunk + bh * p.kv_bh + tt * p.kv_blk;
+      const int64_t idx = ahead.c * p.kv_chunk + bh * p.kv_bh + ahead.t * p.kv_blk;
       sk = p.ks[idx];
       sv = p.vs[idx];
+      ahead.next(p);
     }
   };
   float cj = 0.f, log2k = 0.f, invk = 0.f;
@@ -444,12 +470,17 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
   if (n_steps > 1) load_step(1, sk_n, sv_n);
 
+  // Rescale threshold: a row's running max m is only raised (and O, l
+  // rescaled) when some row of this warp would grow by more than tau; until
+  // then p = 2^(s c - m) may reach 2^tau, so P carries an extra 2^-tau.
+  const float tau = p.rescale_tau;
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
+  StepCursor cur;  // K/V tile of step j
   for (int j = 0; j < n_steps; ++j) {
-    int c, tt, valid;
-    bool extra;
-    step_info(p, j, c, tt, valid, extra);
+    const bool extra = p.has_extra && j == p.n_main_tiles;
+    const int tt = cur.t;
+    const int valid = extra ? kTile : cur.valid(p);
     if (tracer) RP_TRACE(100 + t, j);
 
     if (!warp_wait(bar.s_full + t, j & 1, bar.abort_flag, p.status, kErrWaitS)) {
@@ -462,6 +493,8 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
 #pragma unroll
     for (int q = 0; q < NC / 32; ++q) tmem_ld32(tS + 32 * q, r[q]);
     tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < NC / 32; ++q) reg_fence(r[q]);
     if (tracer) RP_TRACE(104 + t, j);
     tc_fence_before();
     __syncwarp();
@@ -516,15 +549,17 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       mx = fmaxf(mx, xch[((j & 1) * 2 + (1 - half)) * kTile + row]);
     }
     if (tracer) RP_TRACE(106 + t, j);
-    const float m_new = fmaxf(m_run, mx * cj);
-    const bool grew = m_new > m_run;
+    // Both warps of a split row pair see the same maxima, so they agree on resc.
+    const float m_cand = fmaxf(m_run, mx * cj);
+    const bool resc = __any_sync(0xffffffffu, m_cand > m_run + tau);
+    const float m_new = resc ? m_cand : m_run;
     const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-    const float alpha = ex2_approx(m_run - m_use);
-    const float noff = log2k - m_use;
+    const float alpha = resc ? ex2_approx(m_run - m_use) : 1.f;
+    const float noff = log2k - tau - m_use;
 
-    // p' = 2^(s * c_j - m + log2 K_j).  Packed f32x2 FMAs form the exponents;
-    // EPOLY of every 8 go through the FMA-pipe polynomial, the rest through
-    // MUFU ex2; the row sum runs on four packed accumulators.
+    // p' = 2^(s * c_j - m + log2 K_j - tau).  Packed f32x2 FMAs form the
+    // exponents; EPOLY of every 8 go through the FMA-pipe polynomial, the
+    // rest through MUFU ex2; the row sum runs on four packed accumulators.
     uint32_t pk[NC / 4];
     uint32_t pl[(PMODE == 1) ? NC / 4 : 1];
     const uint64_t c2 = pack_f32x2(cj, cj);
@@ -590,10 +625,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     fence_proxy_async_smem();
     if (tracer) RP_TRACE(20 + t, j);
 
-    // O needs rescaling only when a row's running max grew; only then must
-    // PV(j-1) have finished before O is touched.  (P buffer j&1 is already
-    // free: S_full(j) was committed after PV(j-2) was issued.)
-    if (j > 0 && __any_sync(0xffffffffu, grew)) {
+    // O is rescaled only when the running max moved; only then must PV(j-1)
+    // have finished before O is touched.  (P buffer j&1 is already free:
+    // S_full(j) was committed after PV(j-2) was issued.)
+    if (j > 0 && resc) {
       if (C::kPBuf == 2 &&
           !warp_wait(bar.o_done + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
         ok = false;
@@ -607,6 +642,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         uint32_t o[32];
         tmem_ld32(tO + 32 * q, o);
         tmem_wait_ld();
+        reg_fence(o);
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           float u0, u1;
@@ -627,6 +663,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     cj = cj_n;
     log2k = log2k_n;
     invk = invk_n;
+    if (!extra) cur.next(p);
   }
 
   // The last PV of this tile signals o_final (single use, so the wait is
@@ -799,7 +836,22 @@ int split_setting() {
   return v;
 }
 
+// Online-softmax rescale threshold in log2 units (0 = rescale on every
+// growth of a row max).  REPERCEP_B200_RESCALE_TAU in [0, 8] overrides the
+// default (read once).
+float rescale_tau_setting() {
+  static const float v = [] {
+    const char* e = std::getenv("REPERCEP_B200_RESCALE_TAU");
+    if (!e) return kDefaultRescaleTau;
+    const float x = static_cast<float>(std::atof(e));
+    return (x >= 0.f && x <= 8.f) ? x : kDefaultRescaleTau;
+  }();
+  return v;
+}
+
 }  // namespace
+
+float attention_rescale_tau() { return rescale_tau_setting(); }
 
 #ifdef RP_PIPELINE_TRACE
 extern "C" int rp_trace_setup(void* buf, int cta_x, int cta_y) {
@@ -811,10 +863,12 @@ extern "C" int rp_trace_setup(void* buf, int cta_x, int cta_y) {
 }
 #endif
 
-cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
-                             int nq, int p_mode, cudaStream_t st) {
+cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& params, int B,
+                             int H, int nq, int p_mode, cudaStream_t st) {
   const int ep = exp_poly_setting();
   const int sp = split_setting();
+  AttnKernelParams p = params;
+  p.rescale_tau = rescale_tau_setting();
   if (nq == 2 && p_mode == 0) {
     if (sp == 2) {
       if (ep == 0) return launch_variant<2, 0, 0, 2>(maps, p, B, H, st);

@@ -150,6 +150,8 @@ int rp_abi_version(void) { return RP_ABI_VERSION; }
 
 const char* rp_last_error(void) { return g_last_error.c_str(); }
 
+float rp_attn_rescale_tau(void) { return rp::attention_rescale_tau(); }
+
 int rp_device_status(int* status, int reset) {
   if (!status) return fail(RP_ERR_INVALID, "status is null");
   int* dummy = nullptr;

@@ -55,6 +55,10 @@ struct AttnKernelParams {
   const float* vsx;
   int kvx_bh, kvx_blk;   // extra scale index = bh*kvx_bh + qtile*kvx_blk
   float sm_scale_log2;   // softmax scale * log2(e)
+  // Online-softmax rescale threshold (log2 units, >= 0): O and the row sum
+  // are rescaled only when some row's max grows by more than this; P is
+  // scaled by 2^-rescale_tau so a stale max never saturates e4m3.
+  float rescale_tau;
   int causal;
   int* status;           // device status word (0 = ok)
 };
@@ -62,6 +66,9 @@ struct AttnKernelParams {
 struct AttnMaps {
   CUtensorMap q, k, v, kx, vx, o;
 };
+
+// Rescale threshold the attention launches use (see rp_attn_rescale_tau).
+float attention_rescale_tau();
 
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
                              int nq, int p_mode, cudaStream_t st);

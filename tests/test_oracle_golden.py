@@ -77,6 +77,27 @@ def test_reference_kernel_within_tolerance_of_dequant_attention(name):
     assert m["max_abs"] <= bound, m
 
 
+@pytest.mark.parametrize("name", sorted(ATTN))
+@pytest.mark.parametrize("tau", [1.0, 2.0])
+def test_tile_loop_rescale_threshold_stays_within_tolerance(name, tau):
+    """The rescale-threshold variant of the loop (the B200 kernel's default
+    schedule) agrees with the reference kernel's output as closely as the
+    parity contract requires, and a threshold of 0 is the reference loop."""
+    c = ATTN[name]
+    B, H, S, D = c["q"].shape
+    causal = bool(c["causal"][0])
+    q8, qs = oq.quantize_with_scales(c["q"], oq.SCALE_PER_BH)
+    k8, ks = oq.quantize_with_scales(c["k"], oq.SCALE_PER_BH)
+    v8, vs = oq.quantize_with_scales(c["v"], oq.SCALE_PER_BH)
+    args = (q8.reshape(B * H, S, D), k8.reshape(B * H, S, D), v8.reshape(B * H, S, D), qs, ks, vs)
+    got = oa.reference_tile_loop(*args, 1 / math.sqrt(D), causal=causal, rescale_tau=tau)
+    m = oa.parity_metrics(got, bf16_bits_to_f32(c["out"]).reshape(B * H, S, D))
+    assert m["cos"] >= 0.9999, m
+    assert m["max_abs"] <= (0.02 * m["max_ref"] if causal else 2e-2), m
+    same = oa.reference_tile_loop(*args, 1 / math.sqrt(D), causal=causal, rescale_tau=0.0)
+    assert (f32_to_bf16_bits(same).reshape(c["out"].shape) == c["out"]).all()
+
+
 def test_e4m3_codec_roundtrip_all_bytes():
     b = np.arange(256, dtype=np.uint8)
     vals = e4m3_decode(b)
