@@ -43,6 +43,7 @@ constexpr int kVSt = 3;
 constexpr int kDefaultExpPoly = 2;
 constexpr int kDefaultRowSplit = 1;
 constexpr float kDefaultRescaleTau = 1.0f;
+constexpr int kDefaultStagger = 2;
 
 // Pipeline tracing (compiled in only with -DRP_PIPELINE_TRACE): one chosen CTA
 // records (SM clock, event << 16 | step) at every barrier hand-off of every
@@ -84,6 +85,7 @@ enum : int {
   kErrWaitEpi = 0x10A,
   kErrWaitOFinal = 0x10B,
   kErrWaitX = 0x10C,
+  kErrWaitStag = 0x10D,
 };
 
 template <int NQ, int PMODE, int NSPLIT = 1>
@@ -105,14 +107,14 @@ struct Cfg {
   static constexpr int kOffX = kOffP + NQ * kPBuf * kPStride;  // row-max / row-sum exchange
   static constexpr int kXBytes = (NSPLIT == 2) ? NQ * 3 * 2 * kTile * 4 : 0;
   static constexpr int kOffBar = kOffX + kXBytes;
-  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ;
+  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ + 8;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Bars {
   uint64_t *q_full, *k_full, *k_empty, *v_full, *v_empty;
-  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *xch;
+  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *xch, *stag;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -134,7 +136,8 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   b.epi = b.o_final + NQ;
   b.fin = b.epi + NQ;
   b.xch = b.fin + 1;  // [NQ][4 lane quarters][3]: row-max (x2 by step parity), row-sum
-  b.tmem_slot = reinterpret_cast<uint32_t*>(b.xch + 12 * NQ);
+  b.stag = b.xch + 12 * NQ;  // [4 lane quarters][2 by step parity]: tile 0 exp done
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.stag + 8);
   b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
   return b;
 }
@@ -557,6 +560,18 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     const float alpha = resc ? ex2_approx(m_run - m_use) : 1.f;
     const float noff = log2k - tau - m_use;
 
+    // Stagger: tile 1's exp phase starts after tile 0's of the same step, so
+    // the two warps sharing an SM sub-partition alternate MUFU-bound and
+    // latency-bound phases.  Tile 0 is never two steps ahead here (its S for
+    // step j+2 is issued only after tile 1's P of step j), so the barrier
+    // pair indexed by step parity is never two phases ahead.
+    const bool stag_step = NQ == 2 && NSPLIT == 1 && (p.stagger == 2 || (p.stagger == 1 && j == 0));
+    if (stag_step && t == 1 &&
+        !warp_wait(bar.stag + 2 * wq + (j & 1), (j >> 1) & 1, bar.abort_flag, p.status, kErrWaitStag)) {
+      ok = false;
+      break;
+    }
+
     // p' = 2^(s * c_j - m + log2 K_j - tau).  Packed f32x2 FMAs form the
     // exponents; EPOLY of every 8 go through the FMA-pipe polynomial, the
     // rest through MUFU ex2; the row sum runs on four packed accumulators.
@@ -587,6 +602,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       }
     }
     if (tracer) RP_TRACE(108 + t, j);
+    if (stag_step && t == 0) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar.stag + 2 * wq + (j & 1));
+    }
     // Next step's constants (their MUFU ops queue behind this step's exps and
     // are consumed a whole step later), then the scale loads for step j+2.
     float cj_n = cj, log2k_n = log2k, invk_n = invk;
@@ -752,6 +771,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
     }
     mbar_init(bar.fin, 1);
     for (int i = 0; i < 12 * NQ; ++i) mbar_init(bar.xch + i, 2);
+    for (int i = 0; i < 8; ++i) mbar_init(bar.stag + i, 1);
     *bar.abort_flag = 0;
     fence_barrier_init();
   }
@@ -836,6 +856,18 @@ int split_setting() {
   return v;
 }
 
+// Exp-phase stagger of the two query tiles (0, 1 or 2).
+// REPERCEP_B200_STAGGER overrides the default (read once).
+int stagger_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_STAGGER");
+    if (!e) return kDefaultStagger;
+    const int x = std::atoi(e);
+    return (x >= 0 && x <= 2) ? x : kDefaultStagger;
+  }();
+  return v;
+}
+
 // Online-softmax rescale threshold in log2 units (0 = rescale on every
 // growth of a row max).  REPERCEP_B200_RESCALE_TAU in [0, 8] overrides the
 // default (read once).
@@ -869,6 +901,7 @@ cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& param
   const int sp = split_setting();
   AttnKernelParams p = params;
   p.rescale_tau = rescale_tau_setting();
+  p.stagger = stagger_setting();
   if (nq == 2 && p_mode == 0) {
     if (sp == 2) {
       if (ep == 0) return launch_variant<2, 0, 0, 2>(maps, p, B, H, st);

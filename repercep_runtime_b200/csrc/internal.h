@@ -59,6 +59,8 @@ struct AttnKernelParams {
   // are rescaled only when some row's max grows by more than this; P is
   // scaled by 2^-rescale_tau so a stale max never saturates e4m3.
   float rescale_tau;
+  // Two-tile exp stagger: 0 off, 1 at the first step only, 2 every step.
+  int stagger;
   int causal;
   int* status;           // device status word (0 = ok)
 };
