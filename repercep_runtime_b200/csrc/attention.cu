@@ -88,7 +88,7 @@ enum : int {
   kErrWaitStag = 0x10D,
 };
 
-template <int NQ, int PMODE, int NSPLIT = 1>
+template <int NQ, int PMODE, int NSPLIT = 1, bool TAB = false>
 struct Cfg {
   static constexpr int kNC = kTile / NSPLIT;                 // S columns per softmax thread
   static constexpr int kWarpsPerTile = 4 * NSPLIT;
@@ -106,7 +106,12 @@ struct Cfg {
   static constexpr int kPStride = kPParts * kTileBytes;
   static constexpr int kOffX = kOffP + NQ * kPBuf * kPStride;  // row-max / row-sum exchange
   static constexpr int kXBytes = (NSPLIT == 2) ? NQ * 3 * 2 * kTile * 4 : 0;
-  static constexpr int kOffBar = kOffX + kXBytes;
+  // Per-step constant table (TAB): 64 bytes of reduction scratch, then one
+  // float4 per K/V step.
+  static constexpr int kOffT = kOffX + kXBytes;
+  static constexpr int kTableSteps = TAB ? ((NSPLIT == 2) ? 1536 : 2048) : 0;
+  static constexpr int kTabBytes = TAB ? 64 + kTableSteps * 16 : 0;
+  static constexpr int kOffBar = kOffT + kTabBytes;
   static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ + 8;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -401,10 +406,10 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
 // [half * kNC, half * kNC + kNC).  With NSPLIT = 2 the two halves swap their
 // partial row maxima through shared memory every step and their partial row
 // sums once at the end.
-template <int NQ, int PMODE, int EPOLY, int NSPLIT>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB>
 __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
                            uint8_t* smem, uint32_t tmem, int n_steps) {
-  using C = Cfg<NQ, PMODE, NSPLIT>;
+  using C = Cfg<NQ, PMODE, NSPLIT, TAB>;
   RP_TRACE_INIT();
   constexpr int NC = C::kNC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -427,25 +432,13 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
 
   const float sq = p.qs[bh * p.qs_bh + q_tile_c * p.qs_blk];
 
-  // Largest V scale this CTA meets (positive floats order like their bits).
-  uint32_t vbits = 0;
-  for (int j = lane; j < p.n_main_tiles; j += 32) {
-    int c, tt, valid;
-    bool extra;
-    step_info(p, j, c, tt, valid, extra);
-    vbits = max(vbits, __float_as_uint(p.vs[c * p.kv_chunk + bh * p.kv_bh + tt * p.kv_blk]));
-  }
-  if (p.has_extra && lane == 0)
-    vbits = max(vbits, __float_as_uint(p.vsx[bh * p.kvx_bh + q_tile_c * p.kvx_blk]));
-  vbits = __reduce_max_sync(0xffffffffu, vbits);
-  const float sv_max = __uint_as_float(vbits);
-  const float inv_svmax = 1.f / sv_max;
-
-  // Per-step constants: c_j (log2-domain score scale), log2 K_j and 1/K_j
-  // (K_j = 448 * sv_j / sv_max, the P scale).  They are formed one step
-  // ahead, after the exp loop, and their scale loads two steps ahead, so no
-  // global load, division or MUFU op sits on the path between two steps.
-  StepCursor ahead;  // K/V tile of the next scale load
+  // Largest V scale this CTA meets (positive floats order like their bits),
+  // and the per-step constants c_j / (sm_scale log2 e sq) = sk_j, log2 K_j
+  // and 1/K_j with K_j = 448 * sv_j / sv_max, the P scale.
+  float sv_max, inv_svmax;
+  float cj = 0.f, log2k = 0.f, invk = 0.f;
+  float sk_n = 0.f, sv_n = 1.f;
+  StepCursor ahead;  // K/V tile of the next scale load (no table)
   auto load_step = [&](int j, float& sk, float& sv) {
     if (p.has_extra && j == p.n_main_tiles) {
       const int idx = bh * p.kvx_bh + q_tile_c * p.kvx_blk;
@@ -458,20 +451,75 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       ahead.next(p);
     }
   };
-  float cj = 0.f, log2k = 0.f, invk = 0.f;
   auto make_consts = [&](float sk, float sv, float& c_out, float& l_out, float& i_out) {
     const float kj = 448.f * sv * inv_svmax;
     c_out = p.sm_scale_log2 * sq * sk;
     l_out = __log2f(kj);
     i_out = __fdividef(1.f, kj);
   };
-  float sk_n = 0.f, sv_n = 1.f;
-  if (n_steps > 0) {
-    float sk0, sv0;
-    load_step(0, sk0, sv0);
-    make_consts(sk0, sv0, cj, log2k, invk);
+  float4* const tab = reinterpret_cast<float4*>(smem + C::kOffT + 64);
+  float4 cst_n = make_float4(0.f, 0.f, 0.f, 0.f);
+  if constexpr (TAB) {
+    // All softmax threads fill the table once (n_steps <= kTableSteps); the
+    // extra (decode) tile belongs to the CTA's only query tile (NQ == 1).
+    constexpr int kN = C::kSoftmaxWarps * 32;
+    float* red = reinterpret_cast<float*>(smem + C::kOffT);
+    const int qt0c = min(static_cast<int>(blockIdx.x) * NQ, p.n_q_tiles - 1);
+    uint32_t vb = 0;
+    for (int j = threadIdx.x; j < n_steps; j += kN) {
+      int c, tt, valid;
+      bool extra;
+      step_info(p, j, c, tt, valid, extra);
+      float sk, sv;
+      if (extra) {
+        const int idx = bh * p.kvx_bh + qt0c * p.kvx_blk;
+        sk = p.ksx[idx];
+        sv = p.vsx[idx];
+      } else {
+        const int64_t idx = c * p.kv_chunk + bh * p.kv_bh + tt * p.kv_blk;
+        sk = p.ks[idx];
+        sv = p.vs[idx];
+      }
+      tab[j] = make_float4(sk, sv, 0.f, 0.f);
+      vb = max(vb, __float_as_uint(sv));
+    }
+    vb = __reduce_max_sync(0xffffffffu, vb);
+    if (lane == 0) red[warp] = __uint_as_float(vb);
+    named_bar_sync(1, kN);
+    vb = 0;
+#pragma unroll
+    for (int w = 0; w < C::kSoftmaxWarps; ++w) vb = max(vb, __float_as_uint(red[w]));
+    sv_max = __uint_as_float(vb);
+    inv_svmax = 1.f / sv_max;
+    for (int j = threadIdx.x; j < n_steps; j += kN) {
+      const float4 e = tab[j];
+      const float kj = 448.f * e.y * inv_svmax;
+      tab[j] = make_float4(p.sm_scale_log2 * e.x, __log2f(kj), __fdividef(1.f, kj), 0.f);
+    }
+    named_bar_sync(1, kN);
+    if (n_steps > 0) cst_n = tab[0];
+  } else {
+    uint32_t vbits = 0;
+    for (int j = lane; j < p.n_main_tiles; j += 32) {
+      int c, tt, valid;
+      bool extra;
+      step_info(p, j, c, tt, valid, extra);
+      vbits = max(vbits, __float_as_uint(p.vs[c * p.kv_chunk + bh * p.kv_bh + tt * p.kv_blk]));
+    }
+    if (p.has_extra && lane == 0)
+      vbits = max(vbits, __float_as_uint(p.vsx[bh * p.kvx_bh + q_tile_c * p.kvx_blk]));
+    vbits = __reduce_max_sync(0xffffffffu, vbits);
+    sv_max = __uint_as_float(vbits);
+    inv_svmax = 1.f / sv_max;
+    // Without the table the constants are formed one step ahead, after the
+    // exp loop, and their scale loads two steps ahead.
+    if (n_steps > 0) {
+      float sk0, sv0;
+      load_step(0, sk0, sv0);
+      make_consts(sk0, sv0, cj, log2k, invk);
+    }
+    if (n_steps > 1) load_step(1, sk_n, sv_n);
   }
-  if (n_steps > 1) load_step(1, sk_n, sv_n);
 
   // Rescale threshold: a row's running max m is only raised (and O, l
   // rescaled) when some row of this warp would grow by more than tau; until
@@ -484,6 +532,13 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     const bool extra = p.has_extra && j == p.n_main_tiles;
     const int tt = cur.t;
     const int valid = extra ? kTile : cur.valid(p);
+    if constexpr (TAB) {
+      const float4 cst = cst_n;
+      if (j + 1 < n_steps) cst_n = tab[j + 1];
+      cj = cst.x * sq;
+      log2k = cst.y;
+      invk = cst.z;
+    }
     if (tracer) RP_TRACE(100 + t, j);
 
     if (!warp_wait(bar.s_full + t, j & 1, bar.abort_flag, p.status, kErrWaitS)) {
@@ -609,8 +664,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     // Next step's constants (their MUFU ops queue behind this step's exps and
     // are consumed a whole step later), then the scale loads for step j+2.
     float cj_n = cj, log2k_n = log2k, invk_n = invk;
-    if (j + 1 < n_steps) make_consts(sk_n, sv_n, cj_n, log2k_n, invk_n);
-    if (j + 2 < n_steps) load_step(j + 2, sk_n, sv_n);
+    if constexpr (!TAB) {
+      if (j + 1 < n_steps) make_consts(sk_n, sv_n, cj_n, log2k_n, invk_n);
+      if (j + 2 < n_steps) load_step(j + 2, sk_n, sv_n);
+    }
     float sum;
     {
       float u0, u1;
@@ -736,14 +793,14 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int NSPLIT>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB>
 __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    const __grid_constant__ CUtensorMap tm_kx,
                    const __grid_constant__ CUtensorMap tm_vx,
                    const __grid_constant__ CUtensorMap tm_o, const AttnKernelParams p) {
-  using C = Cfg<NQ, PMODE, NSPLIT>;
+  using C = Cfg<NQ, PMODE, NSPLIT, TAB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -801,7 +858,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   } else if (warp == C::kMmaWarp) {
     if (lane == 0) mma_issuer<NQ, PMODE>(p, bar, smem, tmem, n_steps);
   } else {
-    softmax_wg<NQ, PMODE, EPOLY, NSPLIT>(&tm_o, p, bar, smem, tmem, n_steps);
+    softmax_wg<NQ, PMODE, EPOLY, NSPLIT, TAB>(&tm_o, p, bar, smem, tmem, n_steps);
   }
 
   tc_fence_before();
@@ -812,11 +869,11 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int NSPLIT>
-cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
-                           cudaStream_t st) {
-  using C = Cfg<NQ, PMODE, NSPLIT>;
-  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, NSPLIT>;
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB>
+cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
+                       cudaStream_t st) {
+  using C = Cfg<NQ, PMODE, NSPLIT, TAB>;
+  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, NSPLIT, TAB>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -831,6 +888,27 @@ cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, 
   const dim3 grid((p.n_q_tiles + NQ - 1) / NQ, B * H);
   kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(m.q, m.k, m.v, m.kx, m.vx, m.o, p);
   return cudaGetLastError();
+}
+
+// Per-step constant table in shared memory (1, default) or constants formed
+// in the step loop (0).  REPERCEP_B200_STEP_TABLE overrides (read once).
+int step_table_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_STEP_TABLE");
+    return (e && std::atoi(e) == 0) ? 0 : 1;
+  }();
+  return v;
+}
+
+// The per-step constant table variant whenever every step fits in it.
+template <int NQ, int PMODE, int EPOLY, int NSPLIT>
+cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
+                           cudaStream_t st) {
+  const int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
+  if (step_table_setting() && n_steps <= Cfg<NQ, PMODE, NSPLIT, true>::kTableSteps &&
+      !(NQ > 1 && p.has_extra))
+    return launch_one<NQ, PMODE, EPOLY, NSPLIT, true>(m, p, B, H, st);
+  return launch_one<NQ, PMODE, EPOLY, NSPLIT, false>(m, p, B, H, st);
 }
 
 // Elements (of every 8) whose exp2 runs on the FMA pipe instead of MUFU.

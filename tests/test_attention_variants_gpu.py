@@ -1,0 +1,41 @@
+"""The attention kernel's alternative schedules, each through the whole GPU
+attention / decode / context-parallel parity suite in a fresh process (the
+library reads these switches once per process):
+
+* REPERCEP_B200_STEP_TABLE=0 -- per-step scale constants formed in the step
+  loop (the path sequences longer than the shared-memory table take);
+* REPERCEP_B200_STAGGER=0 -- the two query tiles' exp phases not staggered;
+* REPERCEP_B200_RESCALE_TAU=0 -- O rescaled on every growth of a row max,
+  as the reference kernel does.
+"""
+
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+SUITE = ["tests/test_attention_gpu.py", "tests/test_decode_gpu.py", "tests/test_context_parallel_gpu.py"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(
+    "switch",
+    ["REPERCEP_B200_STEP_TABLE=0", "REPERCEP_B200_STAGGER=0", "REPERCEP_B200_RESCALE_TAU=0"],
+)
+def test_attention_suite_under_schedule_switch(switch):
+    key, value = switch.split("=")
+    env = dict(os.environ, **{key: value})
+    proc = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", *SUITE],
+        cwd=REPO,
+        env=env,
+        capture_output=True,
+        text=True,
+        timeout=900,
+    )
+    assert proc.returncode == 0, proc.stdout[-4000:] + proc.stderr[-2000:]
