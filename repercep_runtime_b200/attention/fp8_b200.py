@@ -9,6 +9,9 @@ calling it while unavailable raises ``RuntimeError`` (reference :114-119).
 The call runs two native launches through librepercep_b200.so: one quantize of
 Q, K and V together, one tcgen05 attention kernel.  There is no fallback
 inside the op — the registry's ``supports()`` chain is where fallback lives.
+Host (CPU) bf16 tensors are also accepted: the call then streams (b, h) chunks
+through the device with copies overlapped with compute
+(``repercep_runtime_b200.streaming``) and returns a host tensor.
 
 Environment switches (read per instance):
   REPERCEP_B200_SCALE_MODE  ``bh`` (default; the reference's per-(b,h) amax) or
@@ -116,10 +119,20 @@ class B200FP8Attention:
                 f"FP8 B200 attention is not available ({self._import_error}). "
                 "Fall back to attention_backend='naive-sdpa'."
             )
+        if query.device.type == "cpu":
+            # Host tensors: copies pipelined with compute, host result returned.
+            from repercep_runtime_b200.streaming import fp8_attention_host
+
+            return fp8_attention_host(
+                query, key, value, causal=causal, scale=scale, scale_mode=self.scale_mode,
+                p_mode=self.p_mode,
+            )
         from repercep_runtime_b200 import ops
 
-        qq, kq, vq = ops.quantize_fp8((query, key, value), scale_mode=self.scale_mode)
-        return ops.attention_fp8_quantized(qq, kq, vq, causal=causal, scale=scale, p_mode=self.p_mode)
+        return ops.fp8_attention(
+            query, key, value, causal=causal, scale=scale, scale_mode=self.scale_mode,
+            p_mode=self.p_mode,
+        )
 
 
 __all__ = ["B200FP8Attention", "b200_device_present"]
