@@ -27,7 +27,7 @@ import torch
 from repercep_runtime_b200 import ops
 
 SLOTS = 3
-TARGET_CHUNKS = 16  # enough to hide the first copy-in and last copy-out
+TARGET_CHUNKS = 32  # small enough to hide the first copy-in and last copy-out
 MIN_CTAS = 148  # one CTA per SM: a chunk should at least fill the GPU once
 
 # One set of streams per device for the life of the process: the caching
