@@ -429,6 +429,66 @@ class Runner:
         return self._op(*dev_inputs)
 
 
+def _event_ms(fn, stream, n: int) -> float:  # type: ignore[no-untyped-def]
+    """Mean device time of `fn` over n calls (after one untimed call)."""
+    import torch
+
+    fn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n):
+        fn()
+    b.record(stream)
+    b.synchronize()
+    return a.elapsed_time(b) / n
+
+
+def side_measurements(runner: Runner, dev, stream, peaks: dict) -> dict:  # type: ignore[no-untyped-def]
+    """Outside the timed region, one GPU only: the quantize kernel's bandwidth
+    and torch's bf16 SDPA on the same inputs (the GPU comparison rows)."""
+    import torch
+    import torch.nn.functional as F
+
+    from repercep_runtime_b200 import ops
+
+    if runner.w["kind"] == "decode" or runner.mode == "cp":
+        return {}
+    out: dict = {}
+    q, k, v = runner.inputs
+    elts = q.numel() + k.numel() + v.numel()
+    ms = _event_ms(lambda: ops.quantize_fp8((q, k, v), scale_mode=runner.scale_mode), stream, 5)
+    algo = 3 * elts  # bf16 read once (2 B) + e4m3 written once (1 B)
+    moved = (5 if runner.scale_mode == ops.SCALE_PER_BH else 3) * elts  # per-(b,h): amax pass reads x again
+    quant = {"ms": ms, "algorithmic_bytes": algo, "achieved_gbs": algo / ms / 1e6,
+             "moved_bytes": moved, "moved_gbs": moved / ms / 1e6, "unit": "GB/s"}
+    if "hbm_gbs" in peaks:
+        quant["peak_gbs"] = float(peaks["hbm_gbs"])
+        quant["frac_moved"] = quant["moved_gbs"] / quant["peak_gbs"]
+        quant["peak_source"] = "of measured"
+    out["quantize"] = quant
+    rows = {}
+    n = 3 if runner.rank_flops > 1e13 else 10
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        backends = [("sdpa_bf16_flash", SDPBackend.FLASH_ATTENTION),
+                    ("sdpa_bf16_cudnn", SDPBackend.CUDNN_ATTENTION)]
+    except Exception:  # pragma: no cover
+        backends = []
+    for name, be in backends:
+        try:
+            with sdpa_kernel(be):
+                ms = _event_ms(lambda: F.scaled_dot_product_attention(q, k, v), stream, n)
+            rows[name] = {"ms": ms, "tflops": runner.rank_flops / (ms / 1e3) / 1e12}
+        except Exception as e:  # backend not available for this shape / build
+            rows[name] = {"unavailable": f"{type(e).__name__}: {str(e)[:120]}"}
+    rows["reference_fp8_triton"] = {"unavailable": "the reference's Triton source does not travel to "
+                                    "the GPU box; its CPU path is the --impl reference arm"}
+    out["gpu_comparison"] = rows
+    torch.cuda.synchronize(dev)
+    return out
+
+
 def dominant_roofline(w: dict, runner: Runner, kernel_ms: float, peaks: dict) -> dict:
     if w["kind"] == "decode":
         C, T, H, P, D = w["C"], w["T"], w["H"], w["P"], w["D"]
@@ -521,6 +581,8 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     ms_step = ms_total / args.steps
     value = runner.job_flops * args.steps / (ms_total / 1e3) / 1e12
 
+    side = side_measurements(runner, dev, stream, load_peaks()) if world == 1 else {}
+
     e2e = None
     if not args.no_e2e:
         host = [x.cpu().pin_memory() for x in runner.inputs]
@@ -593,6 +655,7 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
         "roofline": dominant_roofline(w, runner, kernel_ms, peaks),
         "cpu_baseline": cpu,
         "e2e": e2e,
+        **side,
         "clocks": clocks,
         "gpu_launches": args.steps * runner.launches_per_step,
         "cuda_graph": graphs is not None,

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define RP_ABI_VERSION 1
+#define RP_ABI_VERSION 2
 
 typedef enum rp_status {
   RP_OK = 0,
@@ -58,6 +58,11 @@ typedef enum rp_p_mode {
   RP_P_E4M3 = 0,      /* P rounded once to e4m3 (reference precision) */
   RP_P_E4M3_HILO = 1  /* P split into e4m3 hi + lo planes, two PV MMAs */
 } rp_p_mode;
+
+typedef enum rp_dtype {
+  RP_DTYPE_BF16 = 0,
+  RP_DTYPE_F16 = 1
+} rp_dtype;
 
 /* ABI version compiled into the library (RP_ABI_VERSION). */
 int rp_abi_version(void);
@@ -92,6 +97,17 @@ int rp_quant_fp8_e4m3(int num_tensors, const void* const* x, const int64_t* stri
                       int S, int D, int scale_mode, void* const* out, float* const* scales,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* rp_quant_fp8_e4m3 for bf16 or fp16 input (in_dtype, an rp_dtype) and
+ * e4m3 rows of out_row_bytes (>= D, multiple of 16; bytes D.. of every row are
+ * written as zero, which pads D = 32 / 64 to the 128-byte rows the attention
+ * kernel reads).  fp16 follows the reference's steps in fp16: amax and its
+ * 1e-6 floor in fp16, scale rounded to fp16 (fp8_flash_attn_hopper.py:374-398
+ * on an fp16 tensor).  rp_quant_fp8_e4m3 is this with bf16 and out_row_bytes = D. */
+int rp_quant_fp8_e4m3_ex(int num_tensors, const void* const* x, const int64_t* strides, int B,
+                         int H, int S, int D, int in_dtype, int scale_mode, void* const* out,
+                         int out_row_bytes, float* const* scales, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of rp_quant_fp8_e4m3 for RP_SCALE_PER_BH (no
  * counterpart in the reference, which always allocates through PyTorch).
  * For callers that cannot provide device memory beyond their inputs and
@@ -113,12 +129,27 @@ int rp_quant_fp8_e4m3_noalloc(int num_tensors, const void* const* x, const int64
  * reference's offs_m >= offs_n).  q8 (B*H, Sq, D), k8/v8 (B*H, Skv, D) e4m3
  * contiguous; qs/ks/vs dequant scales in `scale_mode` layout; out bf16
  * (B,H,Sq,D) addressed by out_strides[4] (elements; last must be 1).
- * sm_scale <= 0 selects 1/sqrt(D).  D must be 128.
+ * sm_scale <= 0 selects 1/sqrt(D).  D must be 128 (other head dims: _ex).
  * Replaces the kernel launch of fp8_flash_attention (fp8_flash_attn_hopper.py:432-586). */
 int rp_attn_fp8_fwd(const void* q8, const void* k8, const void* v8, const float* qs,
                     const float* ks, const float* vs, int scale_mode, int B, int H, int Sq,
                     int Skv, int D, float sm_scale, int causal, int p_mode, void* out,
                     const int64_t* out_strides, void* stream);
+
+/* rp_attn_fp8_fwd for every head dim the reference's op advertises
+ * (fp8_hopper_triton.py:41: 32, 64, 128, 256) and both output dtypes.
+ *   qkv_row_bytes  e4m3 row pitch of q8/k8/v8: 128 for D <= 128 (rows of
+ *                  D = 32 / 64 zero-padded to 128 bytes, as
+ *                  rp_quant_fp8_e4m3_ex(out_row_bytes = 128) writes them),
+ *                  256 for D = 256
+ *   out_dtype      RP_DTYPE_BF16 or RP_DTYPE_F16 (the reference returns the
+ *                  query's dtype, fp8_flash_attn_hopper.py:586); out has D
+ *                  columns, strides multiples of 8 elements
+ * sm_scale <= 0 selects 1/sqrt(D) for the true D. */
+int rp_attn_fp8_fwd_ex(const void* q8, const void* k8, const void* v8, const float* qs,
+                       const float* ks, const float* vs, int scale_mode, int B, int H, int Sq,
+                       int Skv, int D, int qkv_row_bytes, float sm_scale, int causal, int p_mode,
+                       void* out, const int64_t* out_strides, int out_dtype, void* stream);
 
 /* Context-parallel variant: K/V arrive as `n_chunks` chunks (one per rank),
  * laid out (n_chunks, B*H, chunk_rows, D) e4m3; every chunk holds chunk_rows

@@ -19,6 +19,8 @@ RP_SCALE_PER_BH = 0
 RP_SCALE_PER_BLOCK128 = 1
 RP_P_E4M3 = 0
 RP_P_E4M3_HILO = 1
+RP_DTYPE_BF16 = 0
+RP_DTYPE_F16 = 1
 
 STATUS_NAMES = {
     -1: "RP_ERR_INVALID",
@@ -63,6 +65,26 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_void_p,
         ],
     ),
+    "rp_quant_fp8_e4m3_ex": (
+        _c_int,
+        [
+            _c_int,
+            ctypes.POINTER(_c_void_p),
+            _c_i64_p,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            ctypes.POINTER(_c_void_p),
+            _c_int,
+            ctypes.POINTER(_c_void_p),
+            _c_void_p,
+            _c_size_t,
+            _c_void_p,
+        ],
+    ),
     "rp_quant_fp8_e4m3_noalloc": (
         _c_int,
         [
@@ -84,6 +106,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         + [_c_int] * 6
         + [_c_float, _c_int, _c_int, _c_void_p, _c_i64_p, _c_void_p],
     ),
+    "rp_attn_fp8_fwd_ex": (
+        _c_int,
+        [_c_void_p] * 6
+        + [_c_int] * 7
+        + [_c_float, _c_int, _c_int, _c_void_p, _c_i64_p, _c_int, _c_void_p],
+    ),
     "rp_attn_fp8_fwd_chunked": (
         _c_int,
         [_c_void_p] * 6
@@ -98,7 +126,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

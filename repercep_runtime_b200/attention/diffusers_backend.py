@@ -35,11 +35,11 @@ def _min_seq_len() -> int:
 def _route_should_use_fp8(query: Any, key: Any, value: Any) -> bool:
     import torch
 
-    if query.dtype != torch.bfloat16:
+    if query.dtype not in (torch.bfloat16, torch.float16):
         return False
     if query.shape != key.shape or query.shape != value.shape:
         return False
-    if query.dim() != 4 or query.shape[-1] != 128:
+    if query.dim() != 4 or query.shape[-1] not in (32, 64, 128, 256):
         return False
     return bool(query.shape[-3] >= _min_seq_len())
 

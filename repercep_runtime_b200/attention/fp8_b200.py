@@ -3,7 +3,8 @@
 
 Same contract: ``name``, ``available`` (never raises; a load failure is kept
 as a string), ``supports(shape, dtype)``, and ``__call__`` on
-(batch, heads, seq, head_dim) bf16 tensors returning the query's dtype;
+(batch, heads, seq, head_dim) bf16 / fp16 tensors (head_dim 32, 64, 128 or 256)
+returning the query's dtype;
 calling it while unavailable raises ``RuntimeError`` (reference :114-119).
 
 The call runs two native launches through librepercep_b200.so: one quantize of
@@ -31,7 +32,7 @@ from repercep_runtime_b200.hardware import DType
 if TYPE_CHECKING:
     import torch
 
-_SUPPORTED_HEAD_DIMS = frozenset({128})
+_SUPPORTED_HEAD_DIMS = frozenset({32, 64, 128, 256})  # as fp8_hopper_triton.py:41
 _SUPPORTED_KINDS = frozenset({AttentionKind.FULL, AttentionKind.CAUSAL})
 
 _SCALE_MODES = {"bh": 0, "per_bh": 0, "block128": 1, "block": 1, "per_block128": 1}
@@ -94,7 +95,7 @@ class B200FP8Attention:
     def supports(self, shape: AttentionShape, dtype: DType) -> bool:
         return (
             self.available
-            and dtype == DType.BF16
+            and dtype in (DType.BF16, DType.FP16)
             and shape.head_dim in _SUPPORTED_HEAD_DIMS
             and shape.kind in _SUPPORTED_KINDS
             and shape.seq_len_q >= 1

@@ -10,7 +10,7 @@
 //                     thread owns one query row == one TMEM lane
 //   warp  4*NQ        TMA producer (Q once, then a ring of K and V tiles)
 //   warp  4*NQ + 1    MMA issuer (one thread issues every tcgen05.mma)
-// TMEM: S[t] at columns [128 t, 128 t + 128), O[t] at [128 (NQ + t), ...).
+// TMEM: S[t] at columns [128 t, 128 t + 128), O[t] at [128 (NQ + DB t), ...) (128 DB wide).
 // SMEM (1024-byte aligned, 128-byte swizzle everywhere):
 //   Q[NQ] | K[3] | V[3] | P[NQ][PBUF] (hi [+ lo] planes) | mbarriers
 // Operand majors: Q, K, P are K-major; V is MN-major (its natural [kv][d]
@@ -88,7 +88,9 @@ enum : int {
   kErrWaitStag = 0x10D,
 };
 
-template <int NQ, int PMODE, int NSPLIT = 1, bool TAB = false>
+// DB: head dim in 128-column blocks (1: D <= 128, the rows of D = 32 / 64
+// zero-padded to 128 bytes; 2: D = 256, one query tile per CTA).
+template <int NQ, int PMODE, int NSPLIT = 1, bool TAB = false, int DB = 1>
 struct Cfg {
   static constexpr int kNC = kTile / NSPLIT;                 // S columns per softmax thread
   static constexpr int kWarpsPerTile = 4 * NSPLIT;
@@ -98,11 +100,16 @@ struct Cfg {
   static constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
   static constexpr int kPBuf = (PMODE == 0) ? 2 : 1;
   static constexpr int kPParts = (PMODE == 0) ? 1 : 2;
-  static constexpr int kTmemCols = (NQ == 2) ? 512 : 256;
+  static_assert(NQ * (1 + DB) * kTile <= 512, "TMEM holds S and O of every query tile");
+  static_assert(DB == 1 || NSPLIT == 1, "row split only for D <= 128");
+  static constexpr int kTmemCols = (NQ * (1 + DB) * kTile > 256) ? 512 : 256;
+  static constexpr int kSt = (DB == 2) ? 2 : 3;       // K and V ring stages (<= kKSt, kVSt)
+  static constexpr int kQBytes = DB * kTileBytes;     // one query tile
+  static constexpr int kKVBytes = DB * kTileBytes;    // one K or V stage
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + NQ * kTileBytes;
-  static constexpr int kOffV = kOffK + kKSt * kTileBytes;
-  static constexpr int kOffP = kOffV + kVSt * kTileBytes;
+  static constexpr int kOffK = kOffQ + NQ * kQBytes;
+  static constexpr int kOffV = kOffK + kSt * kKVBytes;
+  static constexpr int kOffP = kOffV + kSt * kKVBytes;
   static constexpr int kPStride = kPParts * kTileBytes;
   static constexpr int kOffX = kOffP + NQ * kPBuf * kPStride;  // row-max / row-sum exchange
   static constexpr int kXBytes = (NSPLIT == 2) ? NQ * 3 * 2 * kTile * 4 : 0;
@@ -192,6 +199,11 @@ __device__ __forceinline__ uint32_t pack_e4m3x4_residual(uint32_t packed, float 
   return pack_e4m3x4(a - f01.x, b - f01.y, c - f23.x, d - f23.y);
 }
 
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -261,18 +273,21 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
 }
 
 // ------------------------------------------------------------ TMA producer
-template <int NQ, int PMODE>
+template <int NQ, int PMODE, int DB>
 __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                          const CUtensorMap* tm_kx, const CUtensorMap* tm_vx,
                          const AttnKernelParams& p, const Bars& bar, uint8_t* smem, int n_steps) {
-  using C = Cfg<NQ, PMODE>;
+  using C = Cfg<NQ, PMODE, 1, false, DB>;
   RP_TRACE_INIT();
   const int bh = blockIdx.y;
   const int qt0 = blockIdx.x * NQ;
-  mbar_arrive_expect_tx(bar.q_full, NQ * kTileBytes);
+  mbar_arrive_expect_tx(bar.q_full, NQ * C::kQBytes);
 #pragma unroll
   for (int t = 0; t < NQ; ++t)
-    tma_load_4d(smem + C::kOffQ + t * kTileBytes, tm_q, bar.q_full, 0, (qt0 + t) * kTile, bh, 0);
+#pragma unroll
+    for (int kb = 0; kb < DB; ++kb)
+      tma_load_4d(smem + C::kOffQ + t * C::kQBytes + kb * kTileBytes, tm_q, bar.q_full, kb * kTile,
+                  (qt0 + t) * kTile, bh, 0);
 
   int nk = 0, nv = 0;
   bool ok = true;
@@ -281,55 +296,62 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
     const bool extra = p.has_extra && j == p.n_main_tiles;
     const int c = cur.c, t = cur.t;
     if (!extra) cur.next(p);
-    const int ks = j % kKSt, ku = j / kKSt;
+    const int ks = j % C::kSt, ku = j / C::kSt;
     if (ku > 0 && !mbar_wait(bar.k_empty + ks, (ku - 1) & 1, bar.abort_flag, p.status,
                              kErrWaitKEmpty)) {
       ok = false;
       break;
     }
-    mbar_arrive_expect_tx(bar.k_full + ks, kTileBytes);
-    if (extra)
-      tma_load_4d(smem + C::kOffK + ks * kTileBytes, tm_kx, bar.k_full + ks, 0, qt0 * kTile, bh, 0);
-    else
-      tma_load_4d(smem + C::kOffK + ks * kTileBytes, tm_k, bar.k_full + ks, 0, t * kTile, bh, c);
+    mbar_arrive_expect_tx(bar.k_full + ks, C::kKVBytes);
+#pragma unroll
+    for (int kb = 0; kb < DB; ++kb) {
+      uint8_t* dst = smem + C::kOffK + ks * C::kKVBytes + kb * kTileBytes;
+      if (extra)
+        tma_load_4d(dst, tm_kx, bar.k_full + ks, kb * kTile, qt0 * kTile, bh, 0);
+      else
+        tma_load_4d(dst, tm_k, bar.k_full + ks, kb * kTile, t * kTile, bh, c);
+    }
     ++nk;
     RP_TRACE(80, j);
-    const int vs = j % kVSt, vu = j / kVSt;
+    const int vs = j % C::kSt, vu = j / C::kSt;
     if (vu > 0 && !mbar_wait(bar.v_empty + vs, (vu - 1) & 1, bar.abort_flag, p.status,
                              kErrWaitVEmpty)) {
       ok = false;
       break;
     }
-    mbar_arrive_expect_tx(bar.v_full + vs, kTileBytes);
-    if (extra)
-      tma_load_4d(smem + C::kOffV + vs * kTileBytes, tm_vx, bar.v_full + vs, 0, qt0 * kTile, bh, 0);
-    else
-      tma_load_4d(smem + C::kOffV + vs * kTileBytes, tm_v, bar.v_full + vs, 0, t * kTile, bh, c);
+    mbar_arrive_expect_tx(bar.v_full + vs, C::kKVBytes);
+#pragma unroll
+    for (int kb = 0; kb < DB; ++kb) {
+      uint8_t* dst = smem + C::kOffV + vs * C::kKVBytes + kb * kTileBytes;
+      if (extra)
+        tma_load_4d(dst, tm_vx, bar.v_full + vs, kb * kTile, qt0 * kTile, bh, 0);
+      else
+        tma_load_4d(dst, tm_v, bar.v_full + vs, kb * kTile, t * kTile, bh, c);
+    }
     ++nv;
     RP_TRACE(81, j);
   }
   if (!ok) {
     // Abort: let every load already issued land before shared memory goes away.
     mbar_drain(bar.q_full, 0);
-    for (int s = 0; s < kKSt; ++s)
-      if (s < nk) mbar_drain(bar.k_full + s, ((nk - 1 - s) / kKSt) & 1);
-    for (int s = 0; s < kVSt; ++s)
-      if (s < nv) mbar_drain(bar.v_full + s, ((nv - 1 - s) / kVSt) & 1);
+    for (int s = 0; s < C::kSt; ++s)
+      if (s < nk) mbar_drain(bar.k_full + s, ((nk - 1 - s) / C::kSt) & 1);
+    for (int s = 0; s < C::kSt; ++s)
+      if (s < nv) mbar_drain(bar.v_full + s, ((nv - 1 - s) / C::kSt) & 1);
   }
 }
 
 // -------------------------------------------------------------- MMA issuer
-template <int NQ, int PMODE>
+template <int NQ, int PMODE, int DB>
 __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& bar,
                                          uint32_t sbase, uint32_t tmem, int i, bool last) {
-  using C = Cfg<NQ, PMODE>;
+  using C = Cfg<NQ, PMODE, 1, false, DB>;
   RP_TRACE_INIT();
   constexpr uint32_t idesc_pv = make_idesc_e4m3(128, 128, 0, 1);
-  const int vsl = i % kVSt;
-  if (!mbar_wait(bar.v_full + vsl, (i / kVSt) & 1, bar.abort_flag, p.status, kErrWaitV))
+  const int vsl = i % C::kSt;
+  if (!mbar_wait(bar.v_full + vsl, (i / C::kSt) & 1, bar.abort_flag, p.status, kErrWaitV))
     return false;
   RP_TRACE(71, i);
-  const uint64_t vd = make_sw128_desc(sbase + C::kOffV + vsl * kTileBytes, kTileBytes, 1024);
 #pragma unroll
   for (int t = 0; t < NQ; ++t) {
     // Two P_full barriers per tile, alternating by step: a softmax warpgroup
@@ -343,14 +365,20 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
     const int pb = (C::kPBuf == 2) ? (i & 1) : 0;
     const uint32_t paddr = sbase + C::kOffP + (t * C::kPBuf + pb) * C::kPStride;
     const uint64_t pd = make_sw128_desc(paddr, 16, 1024);
-    const uint32_t d_tmem = tmem + (NQ + t) * kTile;
+    // O_t: DB column blocks of 128 after the NQ S tiles; V block nb feeds block nb.
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      mma_f8(d_tmem, pd + 2 * k, vd + 256 * k, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
-    if constexpr (PMODE == 1) {
-      const uint64_t pl = make_sw128_desc(paddr + kTileBytes, 16, 1024);
+    for (int nb = 0; nb < DB; ++nb) {
+      const uint64_t vd = make_sw128_desc(
+          sbase + C::kOffV + vsl * C::kKVBytes + nb * kTileBytes, kTileBytes, 1024);
+      const uint32_t d_tmem = tmem + (NQ + t * DB + nb) * kTile;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) mma_f8(d_tmem, pl + 2 * k, vd + 256 * k, idesc_pv, 1u);
+      for (int k = 0; k < 4; ++k)
+        mma_f8(d_tmem, pd + 2 * k, vd + 256 * k, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+      if constexpr (PMODE == 1) {
+        const uint64_t pl = make_sw128_desc(paddr + kTileBytes, 16, 1024);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mma_f8(d_tmem, pl + 2 * k, vd + 256 * k, idesc_pv, 1u);
+      }
     }
     mma_commit(bar.o_done + t);
     if (last) mma_commit(bar.o_final + t);
@@ -360,22 +388,21 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
   return true;
 }
 
-template <int NQ, int PMODE>
+template <int NQ, int PMODE, int DB>
 __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* smem,
                            uint32_t tmem, int n_steps) {
-  using C = Cfg<NQ, PMODE>;
+  using C = Cfg<NQ, PMODE, 1, false, DB>;
   RP_TRACE_INIT();
   constexpr uint32_t idesc_qk = make_idesc_e4m3(128, 128, 0, 0);
   const uint32_t sbase = smem_u32(smem);
   bool ok = mbar_wait(bar.q_full, 0, bar.abort_flag, p.status, kErrWaitQ);
   for (int j = 0; ok && j < n_steps; ++j) {
-    const int ks = j % kKSt;
-    if (!mbar_wait(bar.k_full + ks, (j / kKSt) & 1, bar.abort_flag, p.status, kErrWaitK)) {
+    const int ks = j % C::kSt;
+    if (!mbar_wait(bar.k_full + ks, (j / C::kSt) & 1, bar.abort_flag, p.status, kErrWaitK)) {
       ok = false;
       break;
     }
     RP_TRACE(75, j);
-    const uint64_t kd = make_sw128_desc(sbase + C::kOffK + ks * kTileBytes, 16, 1024);
 #pragma unroll
     for (int t = 0; t < NQ; ++t) {
       if (j > 0 &&
@@ -384,18 +411,25 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
         break;
       }
       tc_fence_after();
-      const uint64_t qd = make_sw128_desc(sbase + C::kOffQ + t * kTileBytes, 16, 1024);
+      // S_t = sum over the DB head-dim blocks of Q_t[kb] K[kb]^T (K = 32 per MMA)
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        mma_f8(tmem + t * kTile, qd + 2 * k, kd + 2 * k, idesc_qk, k > 0 ? 1u : 0u);
+      for (int kb = 0; kb < DB; ++kb) {
+        const uint64_t kd =
+            make_sw128_desc(sbase + C::kOffK + ks * C::kKVBytes + kb * kTileBytes, 16, 1024);
+        const uint64_t qd =
+            make_sw128_desc(sbase + C::kOffQ + t * C::kQBytes + kb * kTileBytes, 16, 1024);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_f8(tmem + t * kTile, qd + 2 * k, kd + 2 * k, idesc_qk, (kb > 0 || k > 0) ? 1u : 0u);
+      }
       mma_commit(bar.s_full + t);
       RP_TRACE(50 + t, j);
     }
     if (!ok) break;
     mma_commit(bar.k_empty + ks);
-    if (j > 0) ok = issue_pv<NQ, PMODE>(p, bar, sbase, tmem, j - 1, false);
+    if (j > 0) ok = issue_pv<NQ, PMODE, DB>(p, bar, sbase, tmem, j - 1, false);
   }
-  if (ok && n_steps > 0) issue_pv<NQ, PMODE>(p, bar, sbase, tmem, n_steps - 1, true);
+  if (ok && n_steps > 0) issue_pv<NQ, PMODE, DB>(p, bar, sbase, tmem, n_steps - 1, true);
   // Everything this thread issued must finish before TMEM is released.
   mma_commit(bar.fin);
   mbar_drain(bar.fin, 0);
@@ -406,10 +440,10 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
 // [half * kNC, half * kNC + kNC).  With NSPLIT = 2 the two halves swap their
 // partial row maxima through shared memory every step and their partial row
 // sums once at the end.
-template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB>
 __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
                            uint8_t* smem, uint32_t tmem, int n_steps) {
-  using C = Cfg<NQ, PMODE, NSPLIT, TAB>;
+  using C = Cfg<NQ, PMODE, NSPLIT, TAB, DB>;
   RP_TRACE_INIT();
   constexpr int NC = C::kNC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -424,7 +458,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   const int q_tile_c = min(q_tile, p.n_q_tiles - 1);
   const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
   const uint32_t tS = tmem + lane_base + t * kTile + col0;
-  const uint32_t tO = tmem + lane_base + (NQ + t) * kTile + col0;
+  const uint32_t tO = tmem + lane_base + (NQ + t * DB) * kTile + col0;
   uint8_t* pbase = smem + C::kOffP + t * C::kPBuf * C::kPStride;
   // exchange slots: [t][parity 0,1 = row max, 2 = row sum][half][row]
   float* xch = reinterpret_cast<float*>(smem + C::kOffX) + t * 3 * 2 * kTile;
@@ -714,7 +748,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       tc_fence_after();
       const uint64_t a2 = pack_f32x2(alpha, alpha);
 #pragma unroll
-      for (int q = 0; q < NC / 32; ++q) {
+      for (int q = 0; q < DB * NC / 32; ++q) {
         uint32_t o[32];
         tmem_ld32(tO + 32 * q, o);
         tmem_wait_ld();
@@ -755,27 +789,54 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
   if (!ok) return;
 
-  // Epilogue: O * (sv_max / 448) / l -> bf16, staged as two 128x64 halves in
-  // this tile's (now idle) Q and P buffers, written by TMA.
+  // Epilogue: O * (sv_max / 448) / l -> bf16 or fp16, staged in this tile's
+  // (now idle) Q and P buffers and written by TMA: 2 DB boxes of 64 columns
+  // in the 128-byte swizzle, or (out_plain, D <= 64) one unswizzled box of D.
   tc_fence_after();
   const float f = (sv_max / 448.f) / l_run;
-  uint8_t* stage[2] = {smem + C::kOffQ + t * kTileBytes, pbase};
-#pragma unroll
-  for (int hh = 0; hh < 2 / NSPLIT; ++hh) {
-    const int h = (NSPLIT == 2) ? half : hh;  // 64-column box this thread fills
-    const uint32_t srow = smem_u32(stage[h]) + row * 128;
+  auto stage_of = [&](int box) -> uint8_t* {
+    return (box & 1) ? pbase + (box >> 1) * kTileBytes
+                     : smem + C::kOffQ + t * C::kQBytes + (box >> 1) * kTileBytes;
+  };
+  auto pack2 = [&](float a, float b) -> uint32_t {
+    return p.out_f16 ? pack_half2(a * f, b * f) : pack_bf16x2(a * f, b * f);
+  };
+  if (NSPLIT == 1 && p.out_plain) {
+    const int ncols = p.out_cols;  // 32 or 64
+    const uint32_t srow = smem_u32(stage_of(0)) + row * ncols * 2;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
-      uint32_t o[32];
-      tmem_ld32(tO + 64 * hh + 32 * cc, o);
-      tmem_wait_ld();
+      if (cc * 32 < ncols) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * cc, o);
+        tmem_wait_ld();
+        reg_fence(o);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int k = cc * 4 + q;
-        const float* v = reinterpret_cast<const float*>(o) + 8 * q;
-        st_shared_v4(srow + ((k ^ (row & 7)) << 4), pack_bf16x2(v[0] * f, v[1] * f),
-                     pack_bf16x2(v[2] * f, v[3] * f), pack_bf16x2(v[4] * f, v[5] * f),
-                     pack_bf16x2(v[6] * f, v[7] * f));
+        for (int q = 0; q < 4; ++q) {
+          const float* v = reinterpret_cast<const float*>(o) + 8 * q;
+          st_shared_v4(srow + (cc * 4 + q) * 16, pack2(v[0], v[1]), pack2(v[2], v[3]),
+                       pack2(v[4], v[5]), pack2(v[6], v[7]));
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int hh = 0; hh < 2 * DB / NSPLIT; ++hh) {
+      const int box = (NSPLIT == 2) ? half : hh;  // 64-column box this thread fills
+      const uint32_t srow = smem_u32(stage_of(box)) + row * 128;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t o[32];
+        tmem_ld32(tO + 64 * hh + 32 * cc, o);
+        tmem_wait_ld();
+        reg_fence(o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int k = cc * 4 + q;
+          const float* v = reinterpret_cast<const float*>(o) + 8 * q;
+          st_shared_v4(srow + ((k ^ (row & 7)) << 4), pack2(v[0], v[1]), pack2(v[2], v[3]),
+                       pack2(v[4], v[5]), pack2(v[6], v[7]));
+        }
       }
     }
   }
@@ -785,22 +846,27 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   if (wq == 0 && lane == 0 && half == 0 && q_tile < p.n_q_tiles) {
     if (mbar_wait(bar.epi + t, 0, bar.abort_flag, p.status, kErrWaitEpi)) {
       const int b = bh / p.H, h = bh % p.H;
-      tma_store_4d(tm_o, stage[0], 0, q_tile * kTile, h, b);
-      tma_store_4d(tm_o, stage[1], 64, q_tile * kTile, h, b);
+      if (NSPLIT == 1 && p.out_plain) {
+        tma_store_4d(tm_o, stage_of(0), 0, q_tile * kTile, h, b);
+      } else {
+#pragma unroll
+        for (int box = 0; box < 2 * DB; ++box)
+          tma_store_4d(tm_o, stage_of(box), box * 64, q_tile * kTile, h, b);
+      }
       tma_store_commit();
       tma_store_wait0();
     }
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB>
 __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    const __grid_constant__ CUtensorMap tm_kx,
                    const __grid_constant__ CUtensorMap tm_vx,
                    const __grid_constant__ CUtensorMap tm_o, const AttnKernelParams p) {
-  using C = Cfg<NQ, PMODE, NSPLIT, TAB>;
+  using C = Cfg<NQ, PMODE, NSPLIT, TAB, DB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -854,11 +920,12 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   }
 
   if (warp == C::kTmaWarp) {
-    if (lane == 0) producer<NQ, PMODE>(&tm_q, &tm_k, &tm_v, &tm_kx, &tm_vx, p, bar, smem, n_steps);
+    if (lane == 0)
+      producer<NQ, PMODE, DB>(&tm_q, &tm_k, &tm_v, &tm_kx, &tm_vx, p, bar, smem, n_steps);
   } else if (warp == C::kMmaWarp) {
-    if (lane == 0) mma_issuer<NQ, PMODE>(p, bar, smem, tmem, n_steps);
+    if (lane == 0) mma_issuer<NQ, PMODE, DB>(p, bar, smem, tmem, n_steps);
   } else {
-    softmax_wg<NQ, PMODE, EPOLY, NSPLIT, TAB>(&tm_o, p, bar, smem, tmem, n_steps);
+    softmax_wg<NQ, PMODE, EPOLY, NSPLIT, TAB, DB>(&tm_o, p, bar, smem, tmem, n_steps);
   }
 
   tc_fence_before();
@@ -869,11 +936,11 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB>
 cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
                        cudaStream_t st) {
-  using C = Cfg<NQ, PMODE, NSPLIT, TAB>;
-  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, NSPLIT, TAB>;
+  using C = Cfg<NQ, PMODE, NSPLIT, TAB, DB>;
+  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, NSPLIT, TAB, DB>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -901,14 +968,14 @@ int step_table_setting() {
 }
 
 // The per-step constant table variant whenever every step fits in it.
-template <int NQ, int PMODE, int EPOLY, int NSPLIT>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, int DB = 1>
 cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
                            cudaStream_t st) {
   const int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
-  if (step_table_setting() && n_steps <= Cfg<NQ, PMODE, NSPLIT, true>::kTableSteps &&
+  if (step_table_setting() && n_steps <= Cfg<NQ, PMODE, NSPLIT, true, DB>::kTableSteps &&
       !(NQ > 1 && p.has_extra))
-    return launch_one<NQ, PMODE, EPOLY, NSPLIT, true>(m, p, B, H, st);
-  return launch_one<NQ, PMODE, EPOLY, NSPLIT, false>(m, p, B, H, st);
+    return launch_one<NQ, PMODE, EPOLY, NSPLIT, true, DB>(m, p, B, H, st);
+  return launch_one<NQ, PMODE, EPOLY, NSPLIT, false, DB>(m, p, B, H, st);
 }
 
 // Elements (of every 8) whose exp2 runs on the FMA pipe instead of MUFU.
@@ -974,12 +1041,18 @@ extern "C" int rp_trace_setup(void* buf, int cta_x, int cta_y) {
 #endif
 
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& params, int B,
-                             int H, int nq, int p_mode, cudaStream_t st) {
+                             int H, int nq, int p_mode, int db, cudaStream_t st) {
   const int ep = exp_poly_setting();
-  const int sp = split_setting();
+  // the row split has no plain-output epilogue and no D = 256 form
+  const int sp = (params.out_plain || db != 1) ? 1 : split_setting();
   AttnKernelParams p = params;
   p.rescale_tau = rescale_tau_setting();
   p.stagger = stagger_setting();
+  if (db == 2) {
+    if (nq != 1) return cudaErrorInvalidValue;
+    return (p_mode == 0) ? launch_variant<1, 0, 2, 1, 2>(maps, p, B, H, st)
+                         : launch_variant<1, 1, 0, 1, 2>(maps, p, B, H, st);
+  }
   if (nq == 2 && p_mode == 0) {
     if (sp == 2) {
       if (ep == 0) return launch_variant<2, 0, 0, 2>(maps, p, B, H, st);

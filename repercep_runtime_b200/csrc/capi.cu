@@ -87,7 +87,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Rank-4 tiled map.  strides[] are byte strides of dims 1..3.  A dimension
 // of extent 1 gets a harmless stride so the encoder's checks pass.
 int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, const uint64_t dims[4],
-             uint64_t strides[3], const uint32_t box[4], const char* what) {
+             uint64_t strides[3], const uint32_t box[4], const char* what,
+             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return fail(RP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
@@ -100,28 +101,35 @@ int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, const uin
   }
   const uint32_t elem_strides[4] = {1, 1, 1, 1};
   CUresult r = fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, elem_strides,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(RP_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
   return RP_OK;
 }
 
-// e4m3 operand stored (chunks, rows_per_chunk, bh, 128): one 128x128 box.
-int make_fp8_map(CUtensorMap* m, const void* base, int rows, int bh, int chunks, const char* what) {
-  const uint64_t dims[4] = {128, (uint64_t)rows, (uint64_t)bh, (uint64_t)chunks};
-  uint64_t strides[3] = {128, (uint64_t)rows * 128, (uint64_t)rows * 128 * bh};
+// e4m3 operand stored (chunks, rows_per_chunk, bh, row_bytes) with row_bytes
+// 128 or 256: 128x128-byte boxes (two per row block when row_bytes = 256).
+int make_fp8_map(CUtensorMap* m, const void* base, int rows, int bh, int chunks, const char* what,
+                 int row_bytes = 128) {
+  const uint64_t rb = static_cast<uint64_t>(row_bytes);
+  const uint64_t dims[4] = {rb, (uint64_t)rows, (uint64_t)bh, (uint64_t)chunks};
+  uint64_t strides[3] = {rb, (uint64_t)rows * rb, (uint64_t)rows * rb * bh};
   const uint32_t box[4] = {128, 128, 1, 1};
   return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, dims, strides, box, what);
 }
 
-// bf16 output (B, H, S, 128) with element strides {sB, sH, sS}: stored as
-// two 64-column boxes per 128-row tile.
+// 16-bit output (B, H, S, D) with element strides {sB, sH, sS}: 64-column
+// boxes in the 128-byte swizzle per 128-row tile for D >= 128, one
+// unswizzled box of all D columns for D = 32 / 64.
 int make_out_map(CUtensorMap* m, void* base, int B, int H, int S, int64_t sB, int64_t sH,
-                 int64_t sS) {
-  const uint64_t dims[4] = {128, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+                 int64_t sS, int D = 128, bool f16 = false) {
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
   uint64_t strides[3] = {(uint64_t)sS * 2, (uint64_t)sH * 2, (uint64_t)sB * 2};
-  const uint32_t box[4] = {64, 128, 1, 1};
-  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, dims, strides, box, "out");
+  const bool plain = D < 128;
+  const uint32_t box[4] = {plain ? (uint32_t)D : 64u, 128, 1, 1};
+  return make_map(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base,
+                  dims, strides, box, "out",
+                  plain ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
@@ -185,6 +193,19 @@ int rp_quant_workspace_bytes(int num_tensors, int B, int H, int S, int D, int sc
 int rp_quant_fp8_e4m3(int num_tensors, const void* const* x, const int64_t* strides, int B, int H,
                       int S, int D, int scale_mode, void* const* out, float* const* scales,
                       void* workspace, size_t workspace_bytes, void* stream) {
+  return rp_quant_fp8_e4m3_ex(num_tensors, x, strides, B, H, S, D, RP_DTYPE_BF16, scale_mode, out,
+                              D, scales, workspace, workspace_bytes, stream);
+}
+
+int rp_quant_fp8_e4m3_ex(int num_tensors, const void* const* x, const int64_t* strides, int B,
+                         int H, int S, int D, int in_dtype, int scale_mode, void* const* out,
+                         int out_row_bytes, float* const* scales, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (in_dtype != RP_DTYPE_BF16 && in_dtype != RP_DTYPE_F16)
+    return fail(RP_ERR_UNSUPPORTED, "input dtype %d is neither bf16 nor fp16", in_dtype);
+  if (out_row_bytes < D || out_row_bytes % 16)
+    return fail(RP_ERR_INVALID, "out_row_bytes %d must be >= D (%d) and a multiple of 16",
+                out_row_bytes, D);
   if (num_tensors < 1 || num_tensors > rp::kMaxQuantJobs)
     return fail(RP_ERR_INVALID, "num_tensors must be 1..3 (got %d)", num_tensors);
   if (!x || !strides || !out || !scales) return fail(RP_ERR_INVALID, "null argument array");
@@ -206,6 +227,8 @@ int rp_quant_fp8_e4m3(int num_tensors, const void* const* x, const int64_t* stri
   a.H = H;
   a.S = S;
   a.D = D;
+  a.in_f16 = (in_dtype == RP_DTYPE_F16) ? 1 : 0;
+  a.out_ld = out_row_bytes;
   a.nblk = ceil_div(S, rp::kQuantRows);
   a.partial = static_cast<uint32_t*>(workspace);
   for (int i = 0; i < num_tensors; ++i) {
@@ -236,7 +259,8 @@ int check_attn_common(const void* q8, const void* k8, const void* v8, const floa
                       const int64_t* out_strides, int n_out_strides) {
   if (!q8 || !k8 || !v8 || !qs || !ks || !vs || !out || !out_strides)
     return fail(RP_ERR_INVALID, "null pointer argument");
-  if (D != 128) return fail(RP_ERR_UNSUPPORTED, "head_dim %d: this kernel is built for 128", D);
+  if (D != 32 && D != 64 && D != 128 && D != 256)
+    return fail(RP_ERR_UNSUPPORTED, "head_dim %d not in {32,64,128,256}", D);
   if (p_mode != RP_P_E4M3 && p_mode != RP_P_E4M3_HILO)
     return fail(RP_ERR_INVALID, "unknown p_mode %d", p_mode);
   if (out_strides[n_out_strides - 1] != 1)
@@ -255,6 +279,9 @@ rp::AttnKernelParams base_params(int H, int Sq, float sm_scale, int D, int* stat
   p.extra_group = 1;
   const float scale = (sm_scale > 0.f) ? sm_scale : 1.0f / std::sqrt(static_cast<float>(D));
   p.sm_scale_log2 = scale * kLog2e;
+  p.out_f16 = 0;
+  p.out_plain = 0;
+  p.out_cols = 128;
   p.status = status;
   return p;
 }
@@ -265,8 +292,27 @@ int rp_attn_fp8_fwd(const void* q8, const void* k8, const void* v8, const float*
                     const float* ks, const float* vs, int scale_mode, int B, int H, int Sq,
                     int Skv, int D, float sm_scale, int causal, int p_mode, void* out,
                     const int64_t* out_strides, void* stream) {
+  if (D != 128) return fail(RP_ERR_UNSUPPORTED, "head_dim %d: rp_attn_fp8_fwd takes 128 (see _ex)", D);
+  return rp_attn_fp8_fwd_ex(q8, k8, v8, qs, ks, vs, scale_mode, B, H, Sq, Skv, D, 128, sm_scale,
+                            causal, p_mode, out, out_strides, RP_DTYPE_BF16, stream);
+}
+
+int rp_attn_fp8_fwd_ex(const void* q8, const void* k8, const void* v8, const float* qs,
+                       const float* ks, const float* vs, int scale_mode, int B, int H, int Sq,
+                       int Skv, int D, int qkv_row_bytes, float sm_scale, int causal, int p_mode,
+                       void* out, const int64_t* out_strides, int out_dtype, void* stream) {
   int rc = check_attn_common(q8, k8, v8, qs, ks, vs, D, p_mode, out, out_strides, 4);
   if (rc != RP_OK) return rc;
+  const int need_row = (D == 256) ? 256 : 128;
+  if (qkv_row_bytes != need_row)
+    return fail(RP_ERR_UNSUPPORTED,
+                "head_dim %d needs e4m3 rows of %d bytes (zero-padded beyond D), got %d", D,
+                need_row, qkv_row_bytes);
+  if (out_dtype != RP_DTYPE_BF16 && out_dtype != RP_DTYPE_F16)
+    return fail(RP_ERR_UNSUPPORTED, "output dtype %d is neither bf16 nor fp16", out_dtype);
+  for (int i = 0; i < 3; ++i)
+    if ((out_strides[i] * 2) % 16 != 0)
+      return fail(RP_ERR_ALIGN, "output strides must be multiples of 8 elements");
   if (B <= 0 || H <= 0 || Sq <= 0 || Skv <= 0)
     return fail(RP_ERR_INVALID, "B, H, Sq, Skv must be positive");
   if ((int64_t)B * H > 65535) return fail(RP_ERR_UNSUPPORTED, "B*H > 65535");
@@ -278,15 +324,20 @@ int rp_attn_fp8_fwd(const void* q8, const void* k8, const void* v8, const float*
 
   const int BH = B * H;
   rp::AttnMaps m;
-  if ((rc = make_fp8_map(&m.q, q8, Sq, BH, 1, "q")) != RP_OK) return rc;
-  if ((rc = make_fp8_map(&m.k, k8, Skv, BH, 1, "k")) != RP_OK) return rc;
-  if ((rc = make_fp8_map(&m.v, v8, Skv, BH, 1, "v")) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.q, q8, Sq, BH, 1, "q", need_row)) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.k, k8, Skv, BH, 1, "k", need_row)) != RP_OK) return rc;
+  if ((rc = make_fp8_map(&m.v, v8, Skv, BH, 1, "v", need_row)) != RP_OK) return rc;
   m.kx = m.k;
   m.vx = m.v;
-  if ((rc = make_out_map(&m.o, out, B, H, Sq, out_strides[0], out_strides[1], out_strides[2])) != RP_OK)
+  const bool f16 = (out_dtype == RP_DTYPE_F16);
+  if ((rc = make_out_map(&m.o, out, B, H, Sq, out_strides[0], out_strides[1], out_strides[2], D,
+                         f16)) != RP_OK)
     return rc;
 
   rp::AttnKernelParams p = base_params(H, Sq, sm_scale, D, status);
+  p.out_f16 = f16 ? 1 : 0;
+  p.out_plain = (D < 128) ? 1 : 0;
+  p.out_cols = D;
   const int nq_blk = ceil_div(Sq, 128), nk_blk = ceil_div(Skv, 128);
   p.n_chunks = 1;
   p.tiles_per_chunk = nk_blk;
@@ -305,7 +356,9 @@ int rp_attn_fp8_fwd(const void* q8, const void* k8, const void* v8, const float*
   p.ksx = ks;
   p.vsx = vs;
   p.causal = causal ? 1 : 0;
-  cudaError_t e = rp::launch_attention(m, p, B, H, 2, p_mode, static_cast<cudaStream_t>(stream));
+  const int db = (D == 256) ? 2 : 1;
+  cudaError_t e = rp::launch_attention(m, p, B, H, db == 2 ? 1 : 2, p_mode, db,
+                                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return RP_OK;
 }
@@ -316,6 +369,7 @@ int rp_attn_fp8_fwd_chunked(const void* q8, const void* k8, const void* v8, cons
                             int p_mode, void* out, const int64_t* out_strides, void* stream) {
   int rc = check_attn_common(q8, k8, v8, qs, ks, vs, D, p_mode, out, out_strides, 4);
   if (rc != RP_OK) return rc;
+  if (D != 128) return fail(RP_ERR_UNSUPPORTED, "head_dim %d: chunked attention takes 128", D);
   if (B <= 0 || H <= 0 || Sq <= 0 || n_chunks <= 0 || chunk_rows <= 0 || last_rows <= 0 ||
       last_rows > chunk_rows)
     return fail(RP_ERR_INVALID, "bad chunked shape");
@@ -354,7 +408,7 @@ int rp_attn_fp8_fwd_chunked(const void* q8, const void* k8, const void* v8, cons
   p.ksx = ks;
   p.vsx = vs;
   p.causal = 0;
-  cudaError_t e = rp::launch_attention(m, p, B, H, 2, p_mode, static_cast<cudaStream_t>(stream));
+  cudaError_t e = rp::launch_attention(m, p, B, H, 2, p_mode, 1, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return RP_OK;
 }
@@ -367,6 +421,7 @@ int rp_attn_fp8_prefix_decode(const void* q8, const void* kp8, const void* vp8,
                               const int64_t* out_strides, void* stream) {
   int rc = check_attn_common(q8, kp8, vp8, qs, kps, vps, D, p_mode, out, out_strides, 3);
   if (rc != RP_OK) return rc;
+  if (D != 128) return fail(RP_ERR_UNSUPPORTED, "head_dim %d: prefix decode takes 128", D);
   if (!kx8 || !vx8 || !kxs || !vxs) return fail(RP_ERR_INVALID, "null suffix argument");
   if (!aligned16(kx8) || !aligned16(vx8)) return fail(RP_ERR_ALIGN, "suffix must be 16-byte aligned");
   if (C <= 0 || T <= 0 || P <= 0 || H <= 0) return fail(RP_ERR_INVALID, "C, T, P, H must be positive");
@@ -408,7 +463,7 @@ int rp_attn_fp8_prefix_decode(const void* q8, const void* kp8, const void* vp8,
   p.kvx_bh = nq_blk;
   p.kvx_blk = 1;
   p.causal = 0;
-  cudaError_t e = rp::launch_attention(m, p, 1, H, 1, p_mode, static_cast<cudaStream_t>(stream));
+  cudaError_t e = rp::launch_attention(m, p, 1, H, 1, p_mode, 1, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return RP_OK;
 }

@@ -17,15 +17,17 @@ constexpr int kQuantThreads = 256;  // threads per quantize CTA
 constexpr int kMaxQuantJobs = 3;    // Q, K, V in one launch
 
 struct QuantJob {
-  const uint16_t* x;   // bf16 input, element (b,h,s,d) at b*sB + h*sH + s*sS + d
+  const uint16_t* x;   // bf16 / fp16 input, element (b,h,s,d) at b*sB + h*sH + s*sS + d
   int64_t sB, sH, sS;  // element strides (d is unit-stride)
-  uint8_t* out;        // e4m3, contiguous (B*H, S, D)
+  uint8_t* out;        // e4m3, (B*H, S) rows of out_ld bytes
   float* scales;       // (B*H,) per-(b,h) or (B*H, nblk) per block
 };
 
 struct QuantArgs {
   QuantJob job[kMaxQuantJobs];
   int B, H, S, D;
+  int in_f16;          // 0: bf16 input, 1: fp16 input
+  int out_ld;          // output row pitch in bytes (>= D, multiple of 16; padding zeroed)
   int nblk;            // ceil(S / 128)
   uint32_t* partial;   // per-(b,h) mode: (njobs, B*H, nblk) partial amax bits
 };
@@ -62,6 +64,9 @@ struct AttnKernelParams {
   // Two-tile exp stagger: 0 off, 1 at the first step only, 2 every step.
   int stagger;
   int causal;
+  // Output: fp16 instead of bf16; out_plain = one unswizzled box of out_cols
+  // (32 or 64) columns instead of 64-column swizzled boxes.
+  int out_f16, out_plain, out_cols;
   int* status;           // device status word (0 = ok)
 };
 
@@ -72,7 +77,9 @@ struct AttnMaps {
 // Rescale threshold the attention launches use (see rp_attn_rescale_tau).
 float attention_rescale_tau();
 
+// nq: query tiles per CTA (1 or 2); db: head dim in 128-column blocks (1, or
+// 2 for D = 256, which needs nq = 1).
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& p, int B, int H,
-                             int nq, int p_mode, cudaStream_t st);
+                             int nq, int p_mode, int db, cudaStream_t st);
 
 }  // namespace rp

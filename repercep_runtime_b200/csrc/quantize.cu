@@ -15,10 +15,15 @@
 // Scale groups: one per (b,h) (the reference) or one per 128-token block of
 // each (b,h) (the per-block extension; the last block of a ragged S is short).
 //
+// fp16 inputs follow the same steps in fp16: amax and its 1e-6 floor in fp16
+// (fp16(1e-6) = 0x0011, a subnormal), scale = fp16_rne(float(amax)/425.6f).
+//
 // The input is read through arbitrary (b,h,s) element strides with d
 // unit-stride, so BHSD and BSHD (diffusers) tensors need no transposing copy.
-// Output is always contiguous (B*H, S, D).
+// Output rows are out_ld bytes apart (out_ld >= D; bytes D..out_ld-1 of every
+// row are written as zero), rows contiguous: (B*H, S, out_ld).
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
 #include "internal.h"
@@ -27,16 +32,44 @@ namespace rp {
 
 namespace {
 
-constexpr uint32_t kAmaxFloorBits = 0x3586u;  // bf16 nearest to 1e-6
-constexpr float kScaleDiv = 425.6f;           // float(0.95 * 448)
+constexpr float kScaleDiv = 425.6f;  // float(0.95 * 448)
 
+// The two 16-bit input formats: bits -> float, the amax floor (the format's
+// value nearest 1e-6), the +inf pattern, and RNE rounding of a float.
+template <bool F16>
+struct Fmt;
+template <>
+struct Fmt<false> {  // bf16
+  static constexpr uint32_t kFloor = 0x3586u;
+  static constexpr uint32_t kInf = 0x7F80u;
+  __device__ static __forceinline__ float lo(uint32_t w) { return __uint_as_float(w << 16); }
+  __device__ static __forceinline__ float hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+  __device__ static __forceinline__ float of(uint32_t bits) { return __uint_as_float(bits << 16); }
+  __device__ static __forceinline__ float round(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+};
+template <>
+struct Fmt<true> {  // fp16
+  static constexpr uint32_t kFloor = 0x0011u;
+  static constexpr uint32_t kInf = 0x7C00u;
+  __device__ static __forceinline__ float lo(uint32_t w) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+  }
+  __device__ static __forceinline__ float hi(uint32_t w) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+  }
+  __device__ static __forceinline__ float of(uint32_t bits) { return lo(bits); }
+  __device__ static __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+};
+
+template <bool F16>
 __device__ __forceinline__ float scale_from_amax_bits(uint32_t amax_bits) {
+  using T = Fmt<F16>;
   uint32_t b = amax_bits;
-  // Clamp to the floor; NaN (bits > 0x7F80) is kept, like torch.clamp.
-  if (b <= 0x7F80u && b < kAmaxFloorBits) b = kAmaxFloorBits;
-  const float a = __uint_as_float(b << 16);
-  const float s = __fdiv_rn(a, kScaleDiv);
-  return __bfloat162float(__float2bfloat16_rn(s));
+  // Clamp to the floor; NaN (bits above +inf) is kept, like torch.clamp.
+  if (b <= T::kInf && b < T::kFloor) b = T::kFloor;
+  return T::round(__fdiv_rn(T::of(b), kScaleDiv));
 }
 
 __device__ __forceinline__ uint32_t quant_byte(float x, float qm) {
@@ -47,23 +80,26 @@ __device__ __forceinline__ uint32_t quant_byte(float x, float qm) {
   return static_cast<uint32_t>(__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3));
 }
 
-// 8 bf16 (one 16-byte vector) -> 8 e4m3 bytes.
+// 8 16-bit values (one 16-byte vector) -> 8 e4m3 bytes.
+template <bool F16>
 __device__ __forceinline__ uint2 quant8(uint4 v, float qm) {
+  using T = Fmt<F16>;
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   uint32_t o[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const uint32_t a = w[2 * i], b = w[2 * i + 1];
-    const uint32_t b0 = quant_byte(__uint_as_float(a << 16), qm);
-    const uint32_t b1 = quant_byte(__uint_as_float(a & 0xFFFF0000u), qm);
-    const uint32_t b2 = quant_byte(__uint_as_float(b << 16), qm);
-    const uint32_t b3 = quant_byte(__uint_as_float(b & 0xFFFF0000u), qm);
+    const uint32_t b0 = quant_byte(T::lo(a), qm);
+    const uint32_t b1 = quant_byte(T::hi(a), qm);
+    const uint32_t b2 = quant_byte(T::lo(b), qm);
+    const uint32_t b3 = quant_byte(T::hi(b), qm);
     o[i] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
   }
   return make_uint2(o[0], o[1]);
 }
 
-// max of |bf16| bit patterns held in a 16-byte vector.
+// max of |x| bit patterns held in a 16-byte vector (bf16 and fp16 alike:
+// non-negative values of both order like their bits, NaN above +inf).
 __device__ __forceinline__ uint32_t absmax8(uint4 v) {
   uint32_t m = __vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu);
   m = __vmaxu2(m, v.z & 0x7FFF7FFFu);
@@ -84,7 +120,7 @@ __device__ __forceinline__ uint32_t block_max(uint32_t v, uint32_t* red) {
 
 // One CTA = one 128-token block of one (b,h) of one job.  D/8 vectors per
 // row, 128 rows: each thread holds D/16 vectors in registers.
-template <int D>
+template <int D, bool F16>
 struct BlockTile {
   static constexpr int kVpr = D / 8;
   static constexpr int kPer = kQuantRows * kVpr / kQuantThreads;
@@ -107,19 +143,26 @@ struct BlockTile {
     return m;
   }
 
-  __device__ __forceinline__ void store(const QuantJob& j, int bh, int S, int s0, int rows,
-                                        float qm) {
-    uint8_t* out = j.out + ((int64_t)bh * S + s0) * D;
+  __device__ __forceinline__ void store(const QuantJob& j, int bh, int S, int ld, int s0,
+                                        int rows, float qm) {
+    uint8_t* out = j.out + ((int64_t)bh * S + s0) * ld;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
       const int idx = threadIdx.x + k * kQuantThreads;
       const int r = idx / kVpr, c = idx % kVpr;
-      if (r < rows) __stcs(reinterpret_cast<uint2*>(out + (int64_t)r * D + c * 8), quant8(v[k], qm));
+      if (r < rows)
+        __stcs(reinterpret_cast<uint2*>(out + (int64_t)r * ld + c * 8), quant8<F16>(v[k], qm));
+    }
+    // zero padding of rows wider than D
+    const int pad = (ld - D) / 8;
+    for (int idx = threadIdx.x; idx < rows * pad; idx += kQuantThreads) {
+      const int r = idx / pad, c = idx % pad;
+      __stcs(reinterpret_cast<uint2*>(out + (int64_t)r * ld + D + c * 8), make_uint2(0, 0));
     }
   }
 };
 
-template <int D>
+template <int D, bool F16>
 __global__ void __launch_bounds__(kQuantThreads) quant_block_kernel(const QuantArgs a) {
   __shared__ uint32_t red[kQuantThreads / 32];
   const QuantJob& j = a.job[blockIdx.z];
@@ -127,15 +170,15 @@ __global__ void __launch_bounds__(kQuantThreads) quant_block_kernel(const QuantA
   const int b = bh / a.H, h = bh % a.H;
   const int s0 = blk * kQuantRows;
   const int rows = min(kQuantRows, a.S - s0);
-  BlockTile<D> t;
+  BlockTile<D, F16> t;
   const uint32_t m = block_max(t.load(j, b, h, s0, rows), red);
-  const float sc = scale_from_amax_bits(m);
+  const float sc = scale_from_amax_bits<F16>(m);
   if (threadIdx.x == 0) j.scales[(int64_t)bh * a.nblk + blk] = sc;
-  t.store(j, bh, a.S, s0, rows, __frcp_rn(sc));
+  t.store(j, bh, a.S, a.out_ld, s0, rows, __frcp_rn(sc));
 }
 
 // Per-(b,h) pass 1: partial amax of one 128-row chunk.
-template <int D>
+template <int D, bool F16>
 __global__ void __launch_bounds__(kQuantThreads) amax_chunk_kernel(const QuantArgs a) {
   __shared__ uint32_t red[kQuantThreads / 32];
   const QuantJob& j = a.job[blockIdx.z];
@@ -156,7 +199,7 @@ __global__ void __launch_bounds__(kQuantThreads) amax_chunk_kernel(const QuantAr
 }
 
 // Per-(b,h) pass 2: reduce the partials of this (b,h), quantize one chunk.
-template <int D>
+template <int D, bool F16>
 __global__ void __launch_bounds__(kQuantThreads) quant_bh_kernel(const QuantArgs a) {
   __shared__ uint32_t red[kQuantThreads / 32];
   const QuantJob& j = a.job[blockIdx.z];
@@ -166,24 +209,30 @@ __global__ void __launch_bounds__(kQuantThreads) quant_bh_kernel(const QuantArgs
   uint32_t m = 0;
   for (int i = threadIdx.x; i < a.nblk; i += kQuantThreads) m = max(m, part[i]);
   m = block_max(m, red);
-  const float sc = scale_from_amax_bits(m);
+  const float sc = scale_from_amax_bits<F16>(m);
   if (blk == 0 && threadIdx.x == 0) j.scales[bh] = sc;
   const int s0 = blk * kQuantRows;
   const int rows = min(kQuantRows, a.S - s0);
-  BlockTile<D> t;
+  BlockTile<D, F16> t;
   t.load(j, b, h, s0, rows);
-  t.store(j, bh, a.S, s0, rows, __frcp_rn(sc));
+  t.store(j, bh, a.S, a.out_ld, s0, rows, __frcp_rn(sc));
 }
 
 }  // namespace
 
-#define RP_DISPATCH_D(KERNEL)                                                        \
+#define RP_DISPATCH_DF(KERNEL, F16)                                                  \
   switch (a.D) {                                                                     \
-    case 32: KERNEL<32><<<grid, kQuantThreads, 0, st>>>(a); break;                  \
-    case 64: KERNEL<64><<<grid, kQuantThreads, 0, st>>>(a); break;                  \
-    case 128: KERNEL<128><<<grid, kQuantThreads, 0, st>>>(a); break;                \
-    case 256: KERNEL<256><<<grid, kQuantThreads, 0, st>>>(a); break;                \
+    case 32: KERNEL<32, F16><<<grid, kQuantThreads, 0, st>>>(a); break;             \
+    case 64: KERNEL<64, F16><<<grid, kQuantThreads, 0, st>>>(a); break;             \
+    case 128: KERNEL<128, F16><<<grid, kQuantThreads, 0, st>>>(a); break;           \
+    case 256: KERNEL<256, F16><<<grid, kQuantThreads, 0, st>>>(a); break;           \
     default: return cudaErrorInvalidValue;                                           \
+  }
+#define RP_DISPATCH_D(KERNEL)        \
+  if (a.in_f16) {                    \
+    RP_DISPATCH_DF(KERNEL, true)     \
+  } else {                           \
+    RP_DISPATCH_DF(KERNEL, false)    \
   }
 
 cudaError_t launch_quant_block(const QuantArgs& a, int njobs, cudaStream_t st) {

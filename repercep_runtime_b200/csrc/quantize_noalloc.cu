@@ -92,6 +92,8 @@ extern "C" int rp_quant_fp8_e4m3_noalloc(int num_tensors, const void* const* x,
   a.H = H;
   a.S = S;
   a.D = D;
+  a.in_f16 = 0;
+  a.out_ld = D;
   a.nblk = nblk;
   for (int i = 0; i < num_tensors; ++i) {
     const int64_t* st = strides + 4 * i;

@@ -56,36 +56,58 @@ def bhsd_shape(x: torch.Tensor, layout: str) -> tuple[int, int, int, int]:
 
 @dataclass
 class Quantized:
-    """An e4m3 tensor (B*H, S, D) contiguous, viewed as (B, H, S, D), with scales."""
+    """An e4m3 tensor (B*H, S, R) contiguous, viewed as (B, H, S, R), with scales.
+
+    ``R`` is the row width in bytes: the head dim ``d``, or 128 for d = 32 / 64
+    (rows zero-padded, the layout the attention kernel reads)."""
 
     data: torch.Tensor
     scales: torch.Tensor
     scale_mode: int
+    d: int = 0
+
+    def __post_init__(self) -> None:
+        if self.d == 0:
+            self.d = int(self.data.shape[-1])
+
+
+_DTYPES = {torch.bfloat16: _lib.RP_DTYPE_BF16, torch.float16: _lib.RP_DTYPE_F16}
+
+
+def attention_row_bytes(head_dim: int) -> int:
+    """e4m3 row width the attention kernel reads for ``head_dim``."""
+    return 128 if head_dim <= 128 else head_dim
 
 
 def quantize_fp8(
     xs: list[torch.Tensor] | tuple[torch.Tensor, ...],
     scale_mode: int = SCALE_PER_BH,
     layout: str = "bhsd",
+    row_bytes: int | None = None,
 ) -> list[Quantized]:
-    """Quantise 1-3 bf16 tensors of one shape in a single native call.
+    """Quantise 1-3 bf16 or fp16 tensors of one shape in a single native call.
 
     Per-(b,h) mode reproduces ``_per_bh_scale`` + ``_quantize`` of the
     reference (``kernels/triton_kernels/fp8_flash_attn_hopper.py:374-398``)
-    bit for bit; per-block mode applies the same formula to every 128-token
-    block of each (b,h).
+    bit for bit, for either input dtype; per-block mode applies the same
+    formula to every 128-token block of each (b,h).  ``row_bytes`` (default D)
+    widens the output rows with zero bytes.
     """
     if not 1 <= len(xs) <= 3:
         raise ValueError("quantize_fp8 takes 1 to 3 tensors")
     lib = _lib.load()
     B, H, S, D = bhsd_shape(xs[0], layout)
+    row = D if row_bytes is None else int(row_bytes)
+    dtype = xs[0].dtype
+    if dtype not in _DTYPES:
+        raise ValueError(f"inputs must be bf16 or fp16, got {dtype}")
     nblk = (S + BLOCK - 1) // BLOCK
     outs, scales, strides = [], [], []
     for i, x in enumerate(xs):
-        _require_cuda(x, f"x[{i}]", torch.bfloat16)
+        _require_cuda(x, f"x[{i}]", dtype)
         if bhsd_shape(x, layout) != (B, H, S, D):
             raise ValueError("all tensors must share one shape")
-        outs.append(torch.empty((B, H, S, D), dtype=FP8, device=x.device))
+        outs.append(torch.empty((B, H, S, row), dtype=FP8, device=x.device))
         shape = (B * H,) if scale_mode == SCALE_PER_BH else (B * H, nblk)
         scales.append(torch.empty(shape, dtype=torch.float32, device=x.device))
         strides.extend(bhsd_strides(x, layout))
@@ -97,7 +119,7 @@ def quantize_fp8(
     ws = None
     if ws_bytes.value:
         ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=xs[0].device)
-    rc = lib.rp_quant_fp8_e4m3(
+    rc = lib.rp_quant_fp8_e4m3_ex(
         len(xs),
         _lib.ptr_array(x.data_ptr() for x in xs),
         _lib.i64_array(strides),
@@ -105,15 +127,17 @@ def quantize_fp8(
         H,
         S,
         D,
+        _DTYPES[dtype],
         scale_mode,
         _lib.ptr_array(o.data_ptr() for o in outs),
+        row,
         _lib.ptr_array(s.data_ptr() for s in scales),
         ws.data_ptr() if ws is not None else None,
         ws_bytes.value,
         _stream(xs[0]),
     )
-    _lib.check("rp_quant_fp8_e4m3", rc)
-    return [Quantized(o, s, scale_mode) for o, s in zip(outs, scales)]
+    _lib.check("rp_quant_fp8_e4m3_ex", rc)
+    return [Quantized(o, s, scale_mode, D) for o, s in zip(outs, scales)]
 
 
 def attention_fp8_quantized(
@@ -126,20 +150,26 @@ def attention_fp8_quantized(
     p_mode: int = P_E4M3,
     out: torch.Tensor | None = None,
     out_layout: str = "bhsd",
+    out_dtype: torch.dtype = torch.bfloat16,
 ) -> torch.Tensor:
-    """FP8 attention on already-quantised operands; bf16 output."""
+    """FP8 attention on already-quantised operands; bf16 (or fp16) output."""
     lib = _lib.load()
-    B, H, Sq, D = q.data.shape
+    B, H, Sq, row = q.data.shape
+    D = q.d
     Skv = k.data.shape[2]
-    if k.data.shape != v.data.shape or k.data.shape[:2] != (B, H) or k.data.shape[3] != D:
+    if k.data.shape != v.data.shape or k.data.shape[:2] != (B, H) or k.data.shape[3] != row:
         raise ValueError("q, k, v shapes are inconsistent")
+    if not (q.d == k.d == v.d):
+        raise ValueError("q, k, v must share a head dim")
     if not (q.scale_mode == k.scale_mode == v.scale_mode):
         raise ValueError("q, k, v must share a scale mode")
     if out is None:
         shape = (B, H, Sq, D) if out_layout == "bhsd" else (B, Sq, H, D)
-        out = torch.empty(shape, dtype=torch.bfloat16, device=q.data.device)
-    _require_cuda(out, "out", torch.bfloat16)
-    rc = lib.rp_attn_fp8_fwd(
+        out = torch.empty(shape, dtype=out_dtype, device=q.data.device)
+    if out.dtype not in _DTYPES:
+        raise ValueError(f"out must be bf16 or fp16, got {out.dtype}")
+    _require_cuda(out, "out", out.dtype)
+    rc = lib.rp_attn_fp8_fwd_ex(
         q.data.data_ptr(),
         k.data.data_ptr(),
         v.data.data_ptr(),
@@ -152,14 +182,16 @@ def attention_fp8_quantized(
         Sq,
         Skv,
         D,
+        row,
         float(scale) if scale is not None else 0.0,
         1 if causal else 0,
         p_mode,
         out.data_ptr(),
         _lib.i64_array(bhsd_strides(out, out_layout)),
+        _DTYPES[out.dtype],
         _stream(q.data),
     )
-    _lib.check("rp_attn_fp8_fwd", rc)
+    _lib.check("rp_attn_fp8_fwd_ex", rc)
     return out
 
 
@@ -178,19 +210,24 @@ def fp8_attention(
     """Quantise Q/K/V (one native call) and run FP8 attention (one more).
 
     Same contract as the reference's ``fp8_flash_attention``
-    (``fp8_flash_attn_hopper.py:432-586``): bf16 in, default scale 1/sqrt(D),
-    output in the query's dtype and layout.
+    (``fp8_flash_attn_hopper.py:432-586``): bf16 or fp16 in, D in
+    {32, 64, 128, 256}, default scale 1/sqrt(D), output in the query's dtype
+    and layout.
     """
     qshape, kshape = bhsd_shape(q, layout), bhsd_shape(k, layout)
     if k.shape != v.shape or qshape[:2] != kshape[:2] or qshape[3] != kshape[3]:
         raise ValueError("q, k, v must share batch, heads and head_dim; k and v one shape")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v must share a dtype")
+    row = attention_row_bytes(qshape[3])
     if q.shape == k.shape:
-        qq, kq, vq = quantize_fp8((q, k, v), scale_mode=scale_mode, layout=layout)
+        qq, kq, vq = quantize_fp8((q, k, v), scale_mode=scale_mode, layout=layout, row_bytes=row)
     else:  # cross-length attention: one quantize call for Q, one for K and V
-        (qq,) = quantize_fp8((q,), scale_mode=scale_mode, layout=layout)
-        kq, vq = quantize_fp8((k, v), scale_mode=scale_mode, layout=layout)
+        (qq,) = quantize_fp8((q,), scale_mode=scale_mode, layout=layout, row_bytes=row)
+        kq, vq = quantize_fp8((k, v), scale_mode=scale_mode, layout=layout, row_bytes=row)
     return attention_fp8_quantized(
-        qq, kq, vq, causal=causal, scale=scale, p_mode=p_mode, out=out, out_layout=layout
+        qq, kq, vq, causal=causal, scale=scale, p_mode=p_mode, out=out, out_layout=layout,
+        out_dtype=q.dtype,
     )
 
 
@@ -316,7 +353,7 @@ def fp8_attention_op(
     scale_mode: int = SCALE_PER_BH,
     p_mode: int = P_E4M3,
 ) -> torch.Tensor:
-    """``torch.ops.repercep_b200.fp8_attention`` — (B,H,S,D) bf16 in/out."""
+    """``torch.ops.repercep_b200.fp8_attention`` — (B,H,S,D) bf16 or fp16 in/out."""
     return fp8_attention(
         q,
         k,
@@ -343,7 +380,7 @@ def fp8_attention_bshd_op(
     scale_mode: int = SCALE_PER_BH,
     p_mode: int = P_E4M3,
 ) -> torch.Tensor:
-    """``torch.ops.repercep_b200.fp8_attention_bshd`` — diffusers (B,S,H,D) in/out."""
+    """``torch.ops.repercep_b200.fp8_attention_bshd`` — diffusers (B,S,H,D) bf16 or fp16 in/out."""
     return fp8_attention(
         q,
         k,

@@ -88,14 +88,17 @@ def fp8_attention_host(
     out: torch.Tensor | None = None,
     plan: ChunkPlan | None = None,
 ) -> torch.Tensor:
-    """FP8 attention of host bf16 (B, H, S, D) tensors; returns a host bf16
-    (B, H, Sq, D) tensor (pinned unless ``out`` is given).  Inputs should be
+    """FP8 attention of host bf16 / fp16 (B, H, S, D) tensors; returns a host
+    (B, H, Sq, D) tensor of the same dtype (pinned unless ``out`` is given).  Inputs should be
     pinned for the copies to overlap; pageable inputs still work, serially."""
     for name, t in (("query", query), ("key", key), ("value", value)):
         if t.device.type != "cpu":
             raise ValueError(f"{name} must be a host tensor (got {t.device})")
-        if t.dtype != torch.bfloat16 or t.dim() != 4:
-            raise ValueError(f"{name} must be a 4-D bf16 tensor (B, H, S, D)")
+        if t.dtype not in (torch.bfloat16, torch.float16) or t.dim() != 4:
+            raise ValueError(f"{name} must be a 4-D bf16 or fp16 tensor (B, H, S, D)")
+    dtype = query.dtype
+    if key.dtype != dtype or value.dtype != dtype:
+        raise ValueError("query, key, value must share a dtype")
     B, H, Sq, D = query.shape
     Skv = key.shape[2]
     if key.shape != value.shape or key.shape[:2] != (B, H) or key.shape[3] != D:
@@ -107,9 +110,9 @@ def fp8_attention_host(
     else:
         dev = torch.device(device)
     if out is None:
-        out = torch.empty((B, H, Sq, D), dtype=torch.bfloat16, pin_memory=True)
-    elif out.shape != (B, H, Sq, D) or out.dtype != torch.bfloat16 or out.device.type != "cpu":
-        raise ValueError("out must be a host bf16 (B, H, Sq, D) tensor")
+        out = torch.empty((B, H, Sq, D), dtype=dtype, pin_memory=True)
+    elif out.shape != (B, H, Sq, D) or out.dtype != dtype or out.device.type != "cpu":
+        raise ValueError("out must be a host (B, H, Sq, D) tensor of the query's dtype")
     bh = B * H
     plan = plan or plan_chunks(bh, Sq)
     q3 = query.reshape(bh, Sq, D)
@@ -123,10 +126,10 @@ def fp8_attention_host(
         c = plan.chunk
         slots = [
             (
-                torch.empty((c, Sq, D), dtype=torch.bfloat16, device=dev),
-                torch.empty((c, Skv, D), dtype=torch.bfloat16, device=dev),
-                torch.empty((c, Skv, D), dtype=torch.bfloat16, device=dev),
-                torch.empty((c, Sq, D), dtype=torch.bfloat16, device=dev),
+                torch.empty((c, Sq, D), dtype=dtype, device=dev),
+                torch.empty((c, Skv, D), dtype=dtype, device=dev),
+                torch.empty((c, Skv, D), dtype=dtype, device=dev),
+                torch.empty((c, Sq, D), dtype=dtype, device=dev),
             )
             for _ in range(min(SLOTS, plan.n))
         ]

@@ -20,7 +20,10 @@ PyTorch's e4m3 conversion -- the conversion the reference's own quantizer
 uses (:398).  Every other interpreter operation is untouched.
 
 Writes tests/golden/quantize_cases.npz and tests/golden/attention_cases.npz:
-bf16 inputs as uint16 bit patterns, fp32 scales, e4m3 bytes, bf16 outputs.
+bf16 inputs as uint16 bit patterns, fp32 scales, e4m3 bytes, bf16 outputs;
+and tests/golden/quantize_f16_cases.npz / attention_extra_cases.npz: the
+quantizer on fp16 inputs, attention at head dims 32, 64, 256 and on fp16
+(outputs in the input's dtype).
 
     python tests/golden/make_golden.py [--reference /root/reference]
 """
@@ -56,19 +59,41 @@ ATTN_CASES = [
     ("n1_1x1x192x128_causal", (1, 1, 192, 128), "n1", 23, True),
 ]
 
+# The other head dims the reference's op advertises (fp8_hopper_triton.py:41)
+# and fp16 inputs (its supports() takes BF16 and FP16), written to separate
+# files so the fixtures above stay byte-identical.
+QUANT_F16_CASES = [
+    ("f16_n1_1x2x300x64", (1, 2, 300, 64), "n1", 31),
+    ("f16_outlier_1x1x257x128", (1, 1, 257, 128), "n1_outlier", 32),
+    ("f16_qkdiv8_1x1x77x32", (1, 1, 77, 32), "qk_div8", 33),
+    ("f16_zeros_1x1x128x64", (1, 1, 128, 64), "zeros", 34),
+    ("f16_tiny_1x2x64x64", (1, 2, 64, 64), "tiny", 35),
+    ("f16_huge_1x1x64x128", (1, 1, 64, 128), "huge", 36),
+    ("f16_naninf_1x2x128x256", (1, 2, 128, 256), "naninf", 37),
+]
 
-def gen(shape, dist, seed):  # type: ignore[no-untyped-def]
+ATTN_EXTRA_CASES = [
+    # (name, (B,H,S,D), dist, seed, causal, dtype)
+    ("n05_1x1x192x64", (1, 1, 192, 64), "n05", 41, False, "bf16"),
+    ("n05_1x1x160x32_causal", (1, 1, 160, 32), "n05", 42, True, "bf16"),
+    ("n05_1x1x144x256", (1, 1, 144, 256), "n05", 43, False, "bf16"),
+    ("f16_n05_1x1x200x128", (1, 1, 200, 128), "n05", 44, False, "f16"),
+]
+
+
+def gen(shape, dist, seed, dtype=None):  # type: ignore[no-untyped-def]
     import torch
 
     from helpers import gen_bf16
 
+    dtype = torch.bfloat16 if dtype is None else dtype
     if dist != "naninf":
-        return gen_bf16(shape, dist, seed)
-    x = gen_bf16(shape, "n1", seed)
+        return gen_bf16(shape, dist, seed, dtype)
+    x = gen_bf16(shape, "n1", seed, dtype)
     x[0, 0, 3, 7] = float("nan")
     x[0, 1, 9, 1] = float("inf")
     x[0, 1, 10, 2] = float("-inf")
-    return x.to(torch.bfloat16)
+    return x.to(dtype)
 
 
 def bits(t):  # type: ignore[no-untyped-def]
@@ -125,6 +150,31 @@ def main() -> None:
         a_out[f"{name}/causal"] = np.array([int(causal)])
         print(f"{name}: out max {float(o.float().abs().max()):.4f}")
     np.savez_compressed(HERE / "attention_cases.npz", **a_out)
+
+    f_out: dict[str, np.ndarray] = {}
+    for name, shape, dist, seed in QUANT_F16_CASES:
+        x = gen(shape, dist, seed, torch.float16)
+        s = _per_bh_scale(x)
+        q = _quantize(x, s)
+        f_out[f"{name}/x"] = bits(x)
+        f_out[f"{name}/scales"] = s.numpy().astype(np.float32)
+        f_out[f"{name}/q"] = q.view(torch.uint8).numpy()
+    np.savez_compressed(HERE / "quantize_f16_cases.npz", **f_out)
+
+    e_out: dict[str, np.ndarray] = {}
+    for name, shape, dist, seed, causal, fmt in ATTN_EXTRA_CASES:
+        dt = torch.float16 if fmt == "f16" else torch.bfloat16
+        q, k, v = (gen(shape, dist, seed + i, dt) for i in range(3))
+        o = fp8_flash_attention(q, k, v, causal=causal)
+        assert o.dtype == dt
+        e_out[f"{name}/q"] = bits(q)
+        e_out[f"{name}/k"] = bits(k)
+        e_out[f"{name}/v"] = bits(v)
+        e_out[f"{name}/out"] = bits(o)
+        e_out[f"{name}/causal"] = np.array([int(causal)])
+        e_out[f"{name}/f16"] = np.array([int(fmt == "f16")])
+        print(f"{name}: out max {float(o.float().abs().max()):.4f}")
+    np.savez_compressed(HERE / "attention_extra_cases.npz", **e_out)
 
 
 if __name__ == "__main__":

@@ -8,8 +8,10 @@ import torch
 DISTS = ("n05", "n1", "n1_outlier", "qk_div8", "zeros", "tiny", "huge")
 
 
-def gen_bf16(shape: tuple[int, ...], dist: str, seed: int) -> torch.Tensor:
-    """bf16 CPU tensor drawn from a named distribution with a fixed seed.
+def gen_bf16(
+    shape: tuple[int, ...], dist: str, seed: int, dtype: torch.dtype = torch.bfloat16
+) -> torch.Tensor:
+    """bf16 (or ``dtype``) CPU tensor drawn from a named distribution with a fixed seed.
 
     n05: N(0, 0.5); n1: N(0, 1); n1_outlier: N(0, 1) with 1 % of entries x20
     (mask from the same generator); qk_div8: N(0, 1) / 8 (the reference's own
@@ -35,11 +37,11 @@ def gen_bf16(shape: tuple[int, ...], dist: str, seed: int) -> torch.Tensor:
         x = torch.randn(shape, generator=g) * 1e30
     else:
         raise ValueError(dist)
-    return x.to(torch.bfloat16)
+    return x.to(dtype)
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
-    """bf16 tensor -> uint16 bit patterns (CPU, contiguous)."""
+    """16-bit (bf16 / fp16) tensor -> uint16 bit patterns (CPU, contiguous)."""
     return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 

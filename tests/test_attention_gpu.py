@@ -177,3 +177,72 @@ def test_attention_cosmos_sampled():
     """Cosmos shape: B=2 H=32 S=57600, N(0,0.5), per-128-block scales."""
     rows = np.r_[0:64, 30000:30064, 57536:57600]
     _sampled_parity(2, 32, 57600, "n05", oq.SCALE_PER_BLOCK128, 0, rows, [0, 63], False)
+
+
+HEAD_DIM_CASES = [
+    # B, H, S, D, dist, causal, mode
+    (1, 2, 300, 64, "n05", False, oq.SCALE_PER_BH),
+    (2, 1, 256, 64, "n1", True, oq.SCALE_PER_BLOCK128),
+    (1, 2, 333, 32, "n05", False, oq.SCALE_PER_BLOCK128),
+    (1, 1, 200, 32, "qk_div8", True, oq.SCALE_PER_BH),
+    (1, 2, 300, 256, "n05", False, oq.SCALE_PER_BH),
+    (1, 1, 384, 256, "n05", True, oq.SCALE_PER_BLOCK128),
+]
+
+
+@pytest.mark.parametrize("case", HEAD_DIM_CASES, ids=lambda c: "-".join(map(str, c)))
+def test_attention_other_head_dims(case):
+    """D = 32 / 64 (rows zero-padded to 128 bytes) and D = 256 (one query tile,
+    two 128-column blocks) against fp32 attention on the dequantised inputs."""
+    B, H, S, D, dist, causal, mode = case
+    q, k, v = (gen_bf16((B, H, S, D), dist, seed=s) for s in (51, 52, 53))
+    out = _run_attention(q, k, v, mode=mode, causal=causal)
+    assert out.shape == (B, H, S, D)
+    q8, qs = _quant_np(q, mode)
+    k8, ks = _quant_np(k, mode)
+    v8, vs = _quant_np(v, mode)
+    ref = oa.attention_dequant(q8, k8, v8, qs, ks, vs, 1 / math.sqrt(D), causal=causal)
+    m = oa.parity_metrics(out.reshape(B * H, S, D), ref)
+    bound = 0.05 * m["max_ref"] if causal else MAX_ABS
+    assert m["cos"] >= MIN_COS and m["max_abs"] <= bound, m
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_attention_f16_in_f16_out(D):
+    """fp16 inputs give an fp16 output (the query's dtype, like the reference)."""
+    from repercep_runtime_b200.attention import B200FP8Attention
+
+    B, H, S = 1, 2, 300
+    q, k, v = (gen_bf16((B, H, S, D), "n05", seed=s, dtype=torch.float16) for s in (61, 62, 63))
+    op = B200FP8Attention(scale_mode=oq.SCALE_PER_BH)
+    out = op(q.cuda(), k.cuda(), v.cuda())
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16 and out.shape == q.shape
+    fq = lambda x: oq.quantize_with_scales(bits(x), oq.SCALE_PER_BH, fmt="f16")  # noqa: E731
+    (q8, qs), (k8, ks), (v8, vs) = fq(q), fq(k), fq(v)
+    r = lambda a: a.reshape(B * H, S, D)  # noqa: E731
+    ref = oa.attention_dequant(r(q8), r(k8), r(v8), qs, ks, vs, 1 / math.sqrt(D))
+    _check(out.float().cpu().numpy().reshape(B * H, S, D), ref)
+
+
+def test_attention_f16_matches_reference_kernel_golden():
+    """The kernel on the reference's own fp16 and D = 32 / 64 / 256 fixtures
+    (tests/golden/attention_extra_cases.npz) within the parity tolerance."""
+    from pathlib import Path
+
+    data = np.load(Path(__file__).resolve().parent / "golden" / "attention_extra_cases.npz")
+    names = sorted({k.split("/")[0] for k in data.files})
+    for name in names:
+        f16 = bool(int(data[f"{name}/f16"][0]))
+        causal = bool(int(data[f"{name}/causal"][0]))
+        dt = torch.float16 if f16 else torch.bfloat16
+        q, k, v = (torch.from_numpy(data[f"{name}/{t}"].view(np.int16)).view(dt) for t in "qkv")
+        from repercep_runtime_b200 import ops
+
+        out = ops.fp8_attention(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+        torch.cuda.synchronize()
+        assert out.dtype == dt
+        ref = torch.from_numpy(data[f"{name}/out"].view(np.int16)).view(dt).float().numpy()
+        m = oa.parity_metrics(out.float().cpu().numpy(), ref)
+        bound = 0.05 * m["max_ref"] if causal else MAX_ABS
+        assert m["cos"] >= 0.999 and m["max_abs"] <= bound, (name, m)

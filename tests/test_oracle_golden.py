@@ -28,6 +28,12 @@ def _cases(fname: str) -> dict[str, dict[str, np.ndarray]]:
 
 QUANT = _cases("quantize_cases.npz")
 ATTN = _cases("attention_cases.npz")
+QUANT_F16 = _cases("quantize_f16_cases.npz")
+ATTN_EXTRA = _cases("attention_extra_cases.npz")
+
+
+def _f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    return np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
 
 
 @pytest.mark.parametrize("name", sorted(QUANT))
@@ -96,6 +102,33 @@ def test_tile_loop_rescale_threshold_stays_within_tolerance(name, tau):
     assert m["max_abs"] <= (0.02 * m["max_ref"] if causal else 2e-2), m
     same = oa.reference_tile_loop(*args, 1 / math.sqrt(D), causal=causal, rescale_tau=0.0)
     assert (f32_to_bf16_bits(same).reshape(c["out"].shape) == c["out"]).all()
+
+
+@pytest.mark.parametrize("name", sorted(QUANT_F16))
+def test_oracle_quantize_f16_matches_reference_bytes(name):
+    """fp16 inputs: the reference's functions run the same steps in fp16."""
+    c = QUANT_F16[name]
+    q, s = oq.quantize_with_scales(c["x"], oq.SCALE_PER_BH, fmt="f16")
+    assert scales_equal(s, c["scales"]).all()
+    assert (q == c["q"]).all(), f"{(q != c['q']).sum()} bytes differ"
+
+
+@pytest.mark.parametrize("name", sorted(ATTN_EXTRA))
+def test_oracle_tile_loop_matches_reference_kernel_other_dims_and_f16(name):
+    """Head dims 32, 64, 256 and fp16 inputs/outputs, bit for bit."""
+    c = ATTN_EXTRA[name]
+    B, H, S, D = c["q"].shape
+    causal = bool(c["causal"][0])
+    fmt = "f16" if int(c["f16"][0]) else "bf16"
+    q8, qs = oq.quantize_with_scales(c["q"], oq.SCALE_PER_BH, fmt)
+    k8, ks = oq.quantize_with_scales(c["k"], oq.SCALE_PER_BH, fmt)
+    v8, vs = oq.quantize_with_scales(c["v"], oq.SCALE_PER_BH, fmt)
+    got = oa.reference_tile_loop(
+        q8.reshape(B * H, S, D), k8.reshape(B * H, S, D), v8.reshape(B * H, S, D), qs, ks, vs,
+        1 / math.sqrt(D), causal=causal,
+    )
+    to_bits = _f32_to_f16_bits if fmt == "f16" else f32_to_bf16_bits
+    assert (to_bits(got).reshape(c["out"].shape) == c["out"]).all()
 
 
 def test_e4m3_codec_roundtrip_all_bytes():

@@ -48,8 +48,11 @@ def test_supports_gates_like_the_reference(monkeypatch):
     op = B200FP8Attention()
     monkeypatch.setattr(op, "_import_error", None)
     assert op.supports(SHAPE, DType.BF16)
-    assert not op.supports(SHAPE, DType.FP16)
-    assert not op.supports(AttentionShape(2, 32, 4096, 4096, 64), DType.BF16)
+    assert op.supports(SHAPE, DType.FP16)
+    assert not op.supports(SHAPE, DType.FP32)
+    for d in (32, 64, 128, 256):  # the reference's head-dim set, fp8_hopper_triton.py:41
+        assert op.supports(AttentionShape(2, 32, 4096, 4096, d), DType.BF16)
+    assert not op.supports(AttentionShape(2, 32, 4096, 4096, 96), DType.BF16)
     assert not op.supports(AttentionShape(2, 32, 4096, 4096, 128, AttentionKind.NEIGHBORHOOD), DType.BF16)
     assert op.supports(AttentionShape(2, 32, 4096, 4096, 128, AttentionKind.CAUSAL), DType.BF16)
     assert not op.supports(AttentionShape(2, 32, 4096, 1024, 128, AttentionKind.CAUSAL), DType.BF16)
@@ -84,9 +87,12 @@ def test_registry_picks_b200_op_when_enabled_and_supported(monkeypatch):
     try:
         op = reg.select_attention_op(B200, SHAPE, DType.BF16)
         assert op.name == "fp8-b200-flash"
-        # other arch / dtype fall through to the floor, like the reference's chain
+        assert reg.select_attention_op(B200, SHAPE, DType.FP16).name == "fp8-b200-flash"
+        # other arch / dtype / head dim fall through to the floor, like the reference's chain
         assert reg.select_attention_op(H100, SHAPE, DType.BF16).name == "naive-sdpa"
-        assert reg.select_attention_op(B200, SHAPE, DType.FP16).name == "naive-sdpa"
+        assert reg.select_attention_op(B200, SHAPE, DType.FP32).name == "naive-sdpa"
+        odd = AttentionShape(2, 32, 4096, 4096, 96)
+        assert reg.select_attention_op(B200, odd, DType.BF16).name == "naive-sdpa"
     finally:
         monkeypatch.delenv("REPERCEP_FP8_ATTENTION")
         importlib.reload(reg)

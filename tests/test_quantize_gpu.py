@@ -115,3 +115,44 @@ def test_quantize_full_cfg2_sampled():
         ref_bytes, ref_scales = oq.quantize_with_scales(xb[bh : bh + 1], oq.SCALE_PER_BH)
         assert scales_equal(sc[bh : bh + 1], ref_scales).all()
         assert bytes_equal_nan_aware(got[bh], ref_bytes.reshape(S, D)).all()
+
+
+F16_CASES = [
+    (1, 2, 300, 64, "n1"),
+    (1, 1, 257, 128, "n1_outlier"),
+    (1, 2, 128, 32, "qk_div8"),
+    (1, 2, 64, 256, "tiny"),    # amax under the fp16 1e-6 floor (subnormals)
+    (1, 1, 64, 128, "huge"),    # overflows fp16 to inf
+    (1, 1, 130, 128, "zeros"),
+]
+
+
+@pytest.mark.parametrize("mode", [oq.SCALE_PER_BH, oq.SCALE_PER_BLOCK128])
+@pytest.mark.parametrize("case", F16_CASES, ids=lambda c: "x".join(map(str, c)))
+def test_quantize_f16_bit_exact(case, mode):
+    """fp16 inputs: bytes and scales equal the oracle's fp16 restatement."""
+    B, H, S, D, dist = case
+    x = gen_bf16((B, H, S, D), dist, seed=12, dtype=torch.float16)
+    ref_bytes, ref_scales = oq.quantize_with_scales(bits(x), mode, fmt="f16")
+    got_bytes, got_scales = _run(x.cuda(), mode, "bhsd")
+    assert scales_equal(got_scales.reshape(ref_scales.shape), ref_scales).all()
+    eq = bytes_equal_nan_aware(got_bytes.reshape(ref_bytes.shape), ref_bytes)
+    assert eq.all(), f"{(~eq).sum()} of {eq.size} bytes differ"
+
+
+@pytest.mark.parametrize("D", [32, 64])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_quantize_padded_rows(D, dtype):
+    """Rows widened to the attention kernel's 128 bytes: data as unpadded, zeros after."""
+    from repercep_runtime_b200 import ops
+
+    x = gen_bf16((2, 3, 200, D), "n1", seed=13, dtype=dtype)
+    fmt = "f16" if dtype == torch.float16 else "bf16"
+    ref_bytes, ref_scales = oq.quantize_with_scales(bits(x), oq.SCALE_PER_BLOCK128, fmt=fmt)
+    (res,) = ops.quantize_fp8([x.cuda()], scale_mode=oq.SCALE_PER_BLOCK128, row_bytes=128)
+    torch.cuda.synchronize()
+    got = fp8_bytes(res.data).reshape(2, 3, 200, 128)
+    assert res.d == D
+    assert scales_equal(res.scales.cpu().numpy().reshape(ref_scales.shape), ref_scales).all()
+    assert bytes_equal_nan_aware(got[..., :D], ref_bytes).all()
+    assert (got[..., D:] == 0).all()
