@@ -12,6 +12,7 @@ src/repercep/attention/diffusers_backend.py:199-212):
   e4m3 K/V (1 byte/element on the wire instead of 2) and the scales over
   NCCL, and each rank runs attention of its own queries against every
   rank's K/V chunk in one kernel launch (``ContextParallelAttention``).
+  The gathers write the kernel's (rank, BH, rows, D) layout directly.
   Slices are whole 128-token blocks (the last rank takes the remainder), so
   every block and its scale are exactly those of the single-GPU per-block
   layout and the result is bit-identical to the single-GPU one.  Each rank
@@ -118,34 +119,41 @@ class ContextParallelAttention:
         self.scale = scale
 
     def gather_kv(self, k8, v8, ks, vs):  # type: ignore[no-untyped-def]
-        """Pad this rank's e4m3 K/V (BH, rows, D) and per-block scales to the
-        common chunk size and all-gather them; returns (n_chunks, BH, chunk_rows, D)
-        K and V and (n_chunks, BH, chunk_rows/128) scales."""
+        """All-gather this rank's e4m3 K/V (BH, rows, D) and per-block scales;
+        returns (n_chunks, BH, chunk_rows, D) K and V and (n_chunks, BH,
+        chunk_rows/128) scales -- the chunked kernel's layout, written by the
+        collectives themselves (K, V and the two scale sets as three gathers).
+        Only a rank whose shard is short of chunk_rows (the last) pads its
+        contribution; nothing is repacked after the gather."""
         import torch
 
         sh = self.shard
         bh, rows, d = k8.shape
         nblk = sh.chunk_rows // BLOCK
         world = sh.world
-        # K, V and both scale tensors travel in one byte buffer per rank.
-        kv_bytes = bh * sh.chunk_rows * d
-        sc_bytes = bh * nblk * 4
-        send = torch.zeros(2 * kv_bytes + 2 * sc_bytes, dtype=torch.uint8, device=k8.device)
-        kv = send[: 2 * kv_bytes].view(2, bh, sh.chunk_rows, d)
-        kv[0, :, :rows].copy_(k8.reshape(bh, rows, d).view(torch.uint8))
-        kv[1, :, :rows].copy_(v8.reshape(bh, rows, d).view(torch.uint8))
-        sc = send[2 * kv_bytes :].view(torch.float32).view(2, bh, nblk)
-        sc[:, :, : ks.shape[-1]].copy_(torch.stack([ks.reshape(bh, -1), vs.reshape(bh, -1)]))
-        recv = torch.empty(world * send.numel(), dtype=torch.uint8, device=k8.device)
         if self.all_gather is None:
             raise RuntimeError("no all_gather bound (world > 1 needs a process group)")
-        self.all_gather(recv, send)
-        per = recv.view(world, -1)
-        kvs = per[:, : 2 * kv_bytes].reshape(world, 2, bh, sh.chunk_rows, d)
-        scs = per[:, 2 * kv_bytes :].contiguous().view(torch.float32).reshape(world, 2, bh, nblk)
-        k_all = kvs[:, 0].contiguous()
-        v_all = kvs[:, 1].contiguous()
-        return k_all, v_all, scs[:, 0].contiguous(), scs[:, 1].contiguous()
+        dev = k8.device
+
+        def padded(x):  # type: ignore[no-untyped-def]
+            if rows == sh.chunk_rows:
+                return x.reshape(bh, rows, d).contiguous()
+            buf = torch.zeros((bh, sh.chunk_rows, d), dtype=torch.uint8, device=dev)
+            buf[:, :rows].copy_(x.reshape(bh, rows, d))
+            return buf
+
+        k_all = torch.empty((world, bh, sh.chunk_rows, d), dtype=torch.uint8, device=dev)
+        v_all = torch.empty_like(k_all)
+        # outputs as (world * BH, rows, D): the rank-major concatenation every
+        # all_gather_into_tensor backend accepts
+        self.all_gather(k_all.view(world * bh, sh.chunk_rows, d), padded(k8))
+        self.all_gather(v_all.view(world * bh, sh.chunk_rows, d), padded(v8))
+        sc = torch.zeros((2, bh, nblk), dtype=torch.float32, device=dev)
+        sc[0, :, : ks.shape[-1]].copy_(ks.reshape(bh, -1))
+        sc[1, :, : vs.shape[-1]].copy_(vs.reshape(bh, -1))
+        sc_all = torch.empty((world, 2, bh, nblk), dtype=torch.float32, device=dev)
+        self.all_gather(sc_all.view(world * 2, bh, nblk), sc)
+        return k_all, v_all, sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous()
 
     def __call__(self, q, k, v, out=None):  # type: ignore[no-untyped-def]
         import torch
