@@ -8,7 +8,7 @@ reference's own ``kernels/cpu/amx_attn/setup.py``, through
 resulting ``oracle/_ref/repercep_amx_ref*.so`` is git-ignored but travels to
 the GPU box, where ``bench.py --impl reference`` times it on the host cores.
 
-    python -m oracle.build_ref [--reference /root/reference]
+    python -m oracle.build_ref [--reference <reference source tree>]
 """
 
 from __future__ import annotations

@@ -1,7 +1,7 @@
 """Generate the golden fixtures that pin the oracle to the reference.
 
-Runs the reference's own code, imported from its source tree (default
-/root/reference, which exists only where the fixtures are generated):
+Runs the reference's own code, imported from its source tree (``--reference``;
+the tree exists only where the fixtures are generated):
 
   * ``_per_bh_scale`` + ``_quantize``
     (kernels/triton_kernels/fp8_flash_attn_hopper.py:374-398) on seeded bf16
@@ -25,7 +25,7 @@ and tests/golden/quantize_f16_cases.npz / attention_extra_cases.npz: the
 quantizer on fp16 inputs, attention at head dims 32, 64, 256 and on fp16
 (outputs in the input's dtype).
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <reference source tree>]
 """
 
 from __future__ import annotations
