@@ -21,13 +21,14 @@ def lib():
 
 def _declared_symbols() -> set[str]:
     text = _lib.HEADER_PATH.read_text()
-    return set(re.findall(r"^\s*(?:int|const char\*)\s+(rp_\w+)\s*\(", text, flags=re.M))
+    return set(re.findall(r"^\s*(?:int|float|const char\*)\s+(rp_\w+)\s*\(", text, flags=re.M))
 
 
 def test_header_declares_the_expected_entry_points():
     syms = _declared_symbols()
-    for name in ("rp_quant_fp8_e4m3", "rp_quant_fp8_e4m3_noalloc", "rp_attn_fp8_fwd",
-                 "rp_attn_fp8_fwd_chunked", "rp_attn_fp8_prefix_decode", "rp_last_error"):
+    for name in ("rp_quant_fp8_e4m3", "rp_quant_fp8_e4m3_ex", "rp_quant_fp8_e4m3_noalloc",
+                 "rp_attn_fp8_fwd", "rp_attn_fp8_fwd_ex", "rp_attn_fp8_fwd_chunked",
+                 "rp_attn_fp8_prefix_decode", "rp_last_error", "rp_attn_rescale_tau"):
         assert name in syms
 
 
@@ -74,3 +75,38 @@ def test_native_error_carries_the_message(lib):
     with pytest.raises(_lib.NativeError, match="RP_ERR_INVALID"):
         _lib.check("rp_quant_workspace_bytes",
                    lib.rp_quant_workspace_bytes(0, 1, 1, 1, 1, 0, ctypes.byref(ctypes.c_size_t())))
+
+
+def test_extended_entry_points_check_dtype_rows_and_head_dim(lib):
+    dummy = 1 << 20
+    strides = _lib.i64_array([0, 0, 0, 1])
+    ptrs = _lib.ptr_array([dummy])
+    # quantizer: unknown input dtype, rows narrower than D or not a multiple of 16
+    rc = lib.rp_quant_fp8_e4m3_ex(1, ptrs, strides, 1, 1, 1, 64, 7, 0, ptrs, 64, ptrs, None, 0, None)
+    assert rc == -2 and b"dtype" in lib.rp_last_error()
+    rc = lib.rp_quant_fp8_e4m3_ex(1, ptrs, strides, 1, 1, 1, 64, 1, 0, ptrs, 32, ptrs, None, 0, None)
+    assert rc == -1 and b"out_row_bytes" in lib.rp_last_error()
+    rc = lib.rp_quant_fp8_e4m3_ex(1, ptrs, strides, 1, 1, 1, 64, 1, 0, ptrs, 136, ptrs, None, 0, None)
+    assert rc == -1 and b"out_row_bytes" in lib.rp_last_error()
+    out_strides = _lib.i64_array([1024, 1024, 64, 1])
+    args = [dummy] * 6
+
+    def attn(D, row, dtype):  # type: ignore[no-untyped-def]
+        return lib.rp_attn_fp8_fwd_ex(*args, 0, 1, 1, 128, 128, D, row, 0.0, 0, 0, dummy,
+                                      out_strides, dtype, None)
+
+    assert attn(96, 128, 0) == -2 and b"head_dim" in lib.rp_last_error()
+    assert attn(64, 64, 0) == -2 and b"128 bytes" in lib.rp_last_error()   # D <= 128 reads 128-byte rows
+    assert attn(256, 128, 0) == -2 and b"256 bytes" in lib.rp_last_error()
+    assert attn(128, 128, 5) == -2 and b"dtype" in lib.rp_last_error()
+    # the plain entry point still takes only D = 128
+    rc = lib.rp_attn_fp8_fwd(*args, 0, 1, 1, 128, 128, 256, 0.0, 0, 0, dummy, out_strides, None)
+    assert rc == -2 and b"_ex" in lib.rp_last_error()
+
+
+def test_rescale_threshold_default(lib, monkeypatch):
+    # read once per process from REPERCEP_B200_RESCALE_TAU; the default is 1
+    import os
+
+    if "REPERCEP_B200_RESCALE_TAU" not in os.environ:
+        assert lib.rp_attn_rescale_tau() == 1.0
