@@ -561,6 +561,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   const float tau = p.rescale_tau;
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
+  if (tracer) RP_TRACE(202 + t, 0);  // softmax prologue (scale table) done
   StepCursor cur;  // K/V tile of step j
   for (int j = 0; j < n_steps; ++j) {
     const bool extra = p.has_extra && j == p.n_main_tiles;
@@ -610,10 +611,12 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       }
     }
     if (extra) {
-      const int g0 = (row / p.extra_group) * p.extra_group;  // own candidate's first token
+      // keep columns [g0, row]: the own candidate's tokens up to this one
+      const int lo = (row / p.extra_group) * p.extra_group - col0;
+      const unsigned span = static_cast<unsigned>(row - col0 - lo);
 #pragma unroll
       for (int i = 0; i < NC; ++i)
-        if (col0 + i < g0 || col0 + i > row) s[i] = -INFINITY;
+        if (static_cast<unsigned>(i - lo) > span) s[i] = -INFINITY;
     }
 
     // Row max: independent chains of 3-input max (16 columns each), a short tree.
@@ -788,6 +791,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     if (ok) l_run += xch[(2 * 2 + (1 - half)) * kTile + row];
   }
   if (!ok) return;
+  if (tracer) RP_TRACE(204 + t, 0);  // last PV done: epilogue starts
 
   // Epilogue: O * (sv_max / 448) / l -> bf16 or fp16, staged in this tile's
   // (now idle) Q and P buffers and written by TMA: 2 DB boxes of 64 columns
@@ -854,7 +858,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
           tma_store_4d(tm_o, stage_of(box), box * 64, q_tile * kTile, h, b);
       }
       tma_store_commit();
-      tma_store_wait0();
+      // Shared memory may be released once the stores have read it; kernel
+      // completion makes the global writes visible.
+      tma_store_wait_read0();
+      if (tracer) RP_TRACE(206 + t, 0);  // output stored
     }
   }
 }
@@ -872,6 +879,8 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const Bars bar = carve_bars<NQ>(smem + C::kOffBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  RP_TRACE_INIT();
+  if (threadIdx.x == 0) RP_TRACE(200, 0);  // kernel entry
 
   if (threadIdx.x == 0) {
     mbar_init(bar.q_full, 1);
@@ -912,6 +921,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *bar.tmem_slot;
+  if (threadIdx.x == 0) RP_TRACE(201, 0);  // barriers and TMEM ready
 
   int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
   if (p.causal) {
