@@ -611,12 +611,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       }
     }
     if (extra) {
-      // keep columns [g0, row]: the own candidate's tokens up to this one
-      const int lo = (row / p.extra_group) * p.extra_group - col0;
-      const unsigned span = static_cast<unsigned>(row - col0 - lo);
+      const int g0 = (row / p.extra_group) * p.extra_group;  // own candidate's first token
 #pragma unroll
       for (int i = 0; i < NC; ++i)
-        if (static_cast<unsigned>(i - lo) > span) s[i] = -INFINITY;
+        if (col0 + i < g0 || col0 + i > row) s[i] = -INFINITY;
     }
 
     // Row max: independent chains of 3-input max (16 columns each), a short tree.
@@ -858,9 +856,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
           tma_store_4d(tm_o, stage_of(box), box * 64, q_tile * kTile, h, b);
       }
       tma_store_commit();
-      // Shared memory may be released once the stores have read it; kernel
-      // completion makes the global writes visible.
-      tma_store_wait_read0();
+      tma_store_wait0();
       if (tracer) RP_TRACE(206 + t, 0);  // output stored
     }
   }
