@@ -2,15 +2,19 @@
 ``"repercep_fp8"`` backend (src/repercep/attention/diffusers_backend.py).
 
 The backend function keeps the reference's signature (:160-171) and routing
-rules (:44, :52-79, :199-231): bf16, q/k/v of one shape, a supported head
-dim, seq_len >= the crossover, no mask / dropout / GQA / context-parallel
-config; everything else goes to a native SDPA fallback.  What changes is the
+rules (:44, :52-79, :199-231): bf16 or fp16, q/k/v of one shape, a head dim
+in {32, 64, 128, 256}, seq_len >= the crossover, no mask / dropout / GQA /
+context-parallel config; everything else goes to a native SDPA fallback.  What changes is the
 layout handling: diffusers passes (B, S, H, D) and the B200 kernels read and
 write that layout through strides, so the reference's three
 ``permute(0, 2, 1, 3).contiguous()`` copies in and one out (:264-267, :286)
 are gone.  The reference's non-finite guard (``isfinite().all()`` per call,
-:271-285) is kept by default because it is part of the seam's contract; set
-``REPERCEP_B200_FINITE_GUARD=0`` to drop its host synchronisation.
+:271-285, falling back to SDPA for that call) is kept by default because it is
+part of the seam's contract, and it costs a host synchronisation per call.
+``REPERCEP_B200_FINITE_GUARD=deferred`` keeps the check on the device instead:
+every call adds "any non-finite output" to a per-device counter without
+synchronising, and ``nonfinite_calls()`` reads it (once per denoise step, say);
+``REPERCEP_B200_FINITE_GUARD=0`` drops the check.
 
 Registration touches diffusers' private registry exactly like the reference
 (:289-339) and is a no-op when diffusers is not installed.
@@ -23,6 +27,38 @@ import os
 from typing import Any
 
 logger = logging.getLogger(__name__)
+
+# per-device count of calls with a non-finite output (deferred guard)
+_NONFINITE: dict[Any, Any] = {}
+
+
+def _guard_mode() -> str:
+    raw = os.environ.get("REPERCEP_B200_FINITE_GUARD", "1").strip().lower()
+    if raw in ("0", "off", "false"):
+        return "off"
+    return "deferred" if raw == "deferred" else "sync"
+
+
+def record_nonfinite(out: Any) -> None:
+    """Add 1 to ``out``'s device counter when ``out`` holds a non-finite
+    value, on the device and without synchronising."""
+    import torch
+
+    cnt = _NONFINITE.get(out.device)
+    if cnt is None:
+        cnt = _NONFINITE[out.device] = torch.zeros((), dtype=torch.int64, device=out.device)
+    cnt.add_((~torch.isfinite(out).all()).to(torch.int64))
+
+
+def nonfinite_calls(reset: bool = False) -> int:
+    """Calls so far (over all devices) whose output held a non-finite value,
+    under the deferred guard.  Synchronises with those devices."""
+    total = 0
+    for cnt in _NONFINITE.values():
+        total += int(cnt.item())
+        if reset:
+            cnt.zero_()
+    return total
 
 REPERCEP_FP8_BACKEND_NAME = "repercep_fp8"
 
@@ -132,7 +168,10 @@ def _repercep_fp8_attention(
         p_mode=op.p_mode,
         layout="bshd",
     )
-    if os.environ.get("REPERCEP_B200_FINITE_GUARD", "1") != "0" and not torch.isfinite(out).all():
+    mode = _guard_mode()
+    if mode == "deferred":
+        record_nonfinite(out)
+    elif mode == "sync" and not torch.isfinite(out).all():
         logger.warning(
             "repercep_fp8: non-finite output at shape %s; falling back to native SDPA",
             tuple(query.shape),

@@ -159,3 +159,24 @@ def test_ops_reject_cpu_tensors():
     x = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16)
     with pytest.raises((ValueError, RuntimeError)):
         ops.quantize_fp8([x])
+
+
+def test_deferred_finite_guard_counts_without_sync(monkeypatch):
+    """The deferred guard adds non-finite calls to a device counter; the
+    count is read once, later (here on CPU tensors)."""
+    from repercep_runtime_b200.attention import diffusers_backend as db
+
+    monkeypatch.setenv("REPERCEP_B200_FINITE_GUARD", "deferred")
+    assert db._guard_mode() == "deferred"
+    db.nonfinite_calls(reset=True)
+    ok = torch.ones(2, 3)
+    bad = torch.ones(2, 3)
+    bad[1, 2] = float("nan")
+    for t in (ok, bad, ok, bad, bad):
+        db.record_nonfinite(t)
+    assert db.nonfinite_calls(reset=True) == 3
+    assert db.nonfinite_calls() == 0
+    monkeypatch.setenv("REPERCEP_B200_FINITE_GUARD", "0")
+    assert db._guard_mode() == "off"
+    monkeypatch.setenv("REPERCEP_B200_FINITE_GUARD", "1")
+    assert db._guard_mode() == "sync"
