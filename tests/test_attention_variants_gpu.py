@@ -6,7 +6,10 @@ library reads these switches once per process):
   loop (the path sequences longer than the shared-memory table take);
 * REPERCEP_B200_STAGGER=0 -- the two query tiles' exp phases not staggered;
 * REPERCEP_B200_RESCALE_TAU=0 -- O rescaled on every growth of a row max,
-  as the reference kernel does.
+  as the reference kernel does;
+* REPERCEP_B200_ROW_SPLIT=2 -- two threads per query row (row max and sum
+  exchanged through shared memory);
+* REPERCEP_B200_EXP_POLY=0 / 4 -- every exp on MUFU / half on the FMA pipe.
 """
 
 from __future__ import annotations
@@ -25,7 +28,14 @@ SUITE = ["tests/test_attention_gpu.py", "tests/test_decode_gpu.py", "tests/test_
 @pytest.mark.gpu
 @pytest.mark.parametrize(
     "switch",
-    ["REPERCEP_B200_STEP_TABLE=0", "REPERCEP_B200_STAGGER=0", "REPERCEP_B200_RESCALE_TAU=0"],
+    [
+        "REPERCEP_B200_STEP_TABLE=0",
+        "REPERCEP_B200_STAGGER=0",
+        "REPERCEP_B200_RESCALE_TAU=0",
+        "REPERCEP_B200_ROW_SPLIT=2",
+        "REPERCEP_B200_EXP_POLY=0",
+        "REPERCEP_B200_EXP_POLY=4",
+    ],
 )
 def test_attention_suite_under_schedule_switch(switch):
     key, value = switch.split("=")
