@@ -179,6 +179,13 @@ def test_attention_cosmos_sampled():
     _sampled_parity(2, 32, 57600, "n05", oq.SCALE_PER_BLOCK128, 0, rows, [0, 63], False)
 
 
+def test_attention_wan_sampled():
+    """Wan shape: B=2 H=40 S=75600 (590 full blocks + an 80-token one),
+    per-block scales; rows at the start, middle and in the ragged last block."""
+    rows = np.r_[0:32, 40000:40032, 75520:75600]
+    _sampled_parity(2, 40, 75600, "n05", oq.SCALE_PER_BLOCK128, 0, rows, [0, 79], False)
+
+
 HEAD_DIM_CASES = [
     # B, H, S, D, dist, causal, mode
     (1, 2, 300, 64, "n05", False, oq.SCALE_PER_BH),
