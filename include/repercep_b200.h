@@ -75,6 +75,14 @@ const char* rp_last_error(void);
  * when `reset` is non-zero it is cleared afterwards.  Diagnostic only. */
 int rp_device_status(int* status, int reset);
 
+/* Diagnostic: one warp waits, bounded by limit_cycles SM cycles (at most the
+ * kernels' own limit), on a barrier nothing arrives on -- the wait every
+ * pipeline role uses -- and records 0x1FF in the device status word when it
+ * runs out, as a timed-out pipeline would.  Shows that a timeout is reported
+ * through rp_device_status and leaves the context usable.  No reference
+ * counterpart. */
+int rp_selftest_wait_timeout(long long limit_cycles, void* stream);
+
 /* Online-softmax rescale threshold (log2 units) the attention kernels use:
  * O and the row sums are rescaled only when a row max grows by more than
  * this, and P is rounded at 2^-tau of its usual scale meanwhile (0 = rescale

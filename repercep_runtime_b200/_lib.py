@@ -42,6 +42,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rp_abi_version": (_c_int, []),
     "rp_last_error": (ctypes.c_char_p, []),
     "rp_attn_rescale_tau": (_c_float, []),
+    "rp_selftest_wait_timeout": (_c_int, [ctypes.c_longlong, _c_void_p]),
     "rp_device_status": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
     "rp_quant_workspace_bytes": (
         _c_int,

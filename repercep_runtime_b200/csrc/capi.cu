@@ -12,6 +12,7 @@
 
 #include "repercep_b200.h"
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace {
 
@@ -152,9 +153,42 @@ int set_last_error(int code, const char* fmt, ...) {
 }
 }  // namespace rp
 
+namespace {
+
+constexpr int kSelftestCode = 0x1FF;
+
+// One warp waits, bounded, on an mbarrier nothing ever arrives on: the same
+// wait every pipeline role uses, run out on purpose.
+__global__ void wait_selftest_kernel(int* status, long long limit) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    rp::mbar_init(&bar, 1);
+    abort_flag = 0;
+    rp::fence_barrier_init();
+  }
+  __syncthreads();
+  rp::mbar_wait(&bar, 0, &abort_flag, status, kSelftestCode, limit);
+  __syncthreads();
+}
+
+}  // namespace
+
 extern "C" {
 
 int rp_abi_version(void) { return RP_ABI_VERSION; }
+
+int rp_selftest_wait_timeout(long long limit_cycles, void* stream) {
+  if (limit_cycles <= 0 || limit_cycles > rp::kWaitLimitCycles)
+    return fail(RP_ERR_INVALID, "limit_cycles must be in (0, %lld]", rp::kWaitLimitCycles);
+  int* status = nullptr;
+  int rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_cycles);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  return RP_OK;
+}
 
 const char* rp_last_error(void) { return g_last_error.c_str(); }
 

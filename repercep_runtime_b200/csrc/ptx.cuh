@@ -60,13 +60,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // role of the CTA; `gerr` is the launch's global status word.  Returns false
 // when the CTA is aborting (this waiter timed out, or another one did).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* gerr, int code) {
+                                          volatile int* abort_flag, int* gerr, int code,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       if (gerr) atomicCAS(gerr, 0, code);
       return false;

@@ -110,3 +110,9 @@ def test_rescale_threshold_default(lib, monkeypatch):
 
     if "REPERCEP_B200_RESCALE_TAU" not in os.environ:
         assert lib.rp_attn_rescale_tau() == 1.0
+
+
+def test_wait_selftest_limit_is_bounded(lib):
+    # checked before any device work: no limit above the kernels' own, none <= 0
+    assert lib.rp_selftest_wait_timeout(0, None) == -1
+    assert lib.rp_selftest_wait_timeout(10**12, None) == -1 and b"limit_cycles" in lib.rp_last_error()
