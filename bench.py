@@ -405,12 +405,14 @@ class Runner:
 
     def host_api(self) -> bool:
         """True when the public op takes this workload's host tensors directly."""
-        return self.w["kind"] != "decode" and self.mode != "cp"
+        return self.w["kind"] != "decode"
 
     def public_call_host(self, host_inputs):  # type: ignore[no-untyped-def]
         """The user-facing call on host tensors (copies pipelined inside)."""
         from repercep_runtime_b200.attention import B200FP8Attention
 
+        if self.mode == "cp":
+            return self.cp(*host_inputs)
         if not hasattr(self, "_op"):
             self._op = B200FP8Attention(scale_mode=self.scale_mode, p_mode=self.args.p_mode)
         return self._op(*host_inputs)
@@ -593,8 +595,8 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             def e2e_step():  # type: ignore[no-untyped-def]
                 runner.public_call_host(host)
 
-            api = ("public op B200FP8Attention.__call__ on pinned host tensors (copies of (b,h) "
-                   "chunks pipelined with compute), host result")
+            api = ("public op (B200FP8Attention / ContextParallelAttention).__call__ on pinned host "
+                   "tensors (copies of (b,h) chunks pipelined with compute), host result")
         else:
             devc = [torch.empty_like(x) for x in runner.inputs]
             out0 = runner.public_call(host, devc)
@@ -605,8 +607,8 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
                     dd.copy_(hh, non_blocking=True)
                 hout.copy_(runner.public_call(host, devc), non_blocking=True)
 
-            api = ("public op __call__ (SharedPrefixFP8Decode / ContextParallelAttention) on "
-                   "pinned host inputs, output copied back")
+            api = ("public op SharedPrefixFP8Decode.__call__ on pinned host inputs, output "
+                   "copied back")
 
         e2e_step()
         torch.cuda.synchronize(dev)

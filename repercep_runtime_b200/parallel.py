@@ -155,7 +155,77 @@ class ContextParallelAttention:
         self.all_gather(sc_all.view(world * 2, bh, nblk), sc)
         return k_all, v_all, sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous()
 
+    def _call_host(self, q, k, v):  # type: ignore[no-untyped-def]
+        """Host (pinned) shards: (b, h) chunks stream through the device with
+        the copies overlapped with quantise + gather + attention, two compute
+        streams taking turns.  Every rank cuts the same chunks (the plan
+        depends on the shared chunk_rows, not on this rank's rows), so the
+        per-chunk collectives line up across ranks."""
+        import torch
+
+        from repercep_runtime_b200 import ops
+        from repercep_runtime_b200.streaming import SLOTS, fp8_attention_host, plan_chunks, _streams
+
+        sh = self.shard
+        B, H, rows, D = q.shape
+        if q.dtype != torch.bfloat16:
+            raise ValueError("context-parallel attention takes bf16 shards")
+        if sh.world == 1:
+            return fp8_attention_host(q, k, v, scale=self.scale, scale_mode=ops.SCALE_PER_BLOCK128,
+                                      p_mode=self.p_mode)
+        bh = B * H
+        plan = plan_chunks(bh, sh.chunk_rows)
+        out = torch.empty((B, H, rows, D), dtype=q.dtype, pin_memory=True)
+        q3, k3, v3 = (t.reshape(bh, rows, D) for t in (q, k, v))
+        o3 = out.view(bh, rows, D)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(dev):
+            caller = torch.cuda.current_stream(dev)
+            h2d, d2h, comp = _streams(dev)
+            c = plan.chunk
+            slots = [
+                tuple(torch.empty((c, rows, D), dtype=q.dtype, device=dev) for _ in range(4))
+                for _ in range(min(SLOTS, plan.n))
+            ]
+            ev_in = [torch.cuda.Event() for _ in slots]
+            ev_comp = [torch.cuda.Event() for _ in slots]
+            ev_out = [torch.cuda.Event() for _ in slots]
+            h2d.wait_stream(caller)
+            for i in range(plan.n):
+                s = i % len(slots)
+                a, b = plan.bounds(i)
+                n = b - a
+                qd, kd, vd, od = slots[s]
+                cs = comp[i % 2]
+                with torch.cuda.stream(h2d):
+                    if i >= len(slots):
+                        h2d.wait_event(ev_comp[s])
+                    qd[:n].copy_(q3[a:b], non_blocking=True)
+                    kd[:n].copy_(k3[a:b], non_blocking=True)
+                    vd[:n].copy_(v3[a:b], non_blocking=True)
+                    ev_in[s].record(h2d)
+                with torch.cuda.stream(cs):
+                    cs.wait_event(ev_in[s])
+                    if i >= len(slots):
+                        cs.wait_event(ev_out[s])
+                    self._device_call(qd[:n].unsqueeze(0), kd[:n].unsqueeze(0), vd[:n].unsqueeze(0),
+                                      out=od[:n].unsqueeze(0))
+                    ev_comp[s].record(cs)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev_comp[s])
+                    o3[a:b].copy_(od[:n], non_blocking=True)
+                    ev_out[s].record(d2h)
+            d2h.synchronize()
+        return out
+
     def __call__(self, q, k, v, out=None):  # type: ignore[no-untyped-def]
+        if q.device.type == "cpu":
+            if out is not None:
+                raise ValueError("host shards return a new host tensor")
+            return self._call_host(q, k, v)
+        return self._device_call(q, k, v, out=out)
+
+    def _device_call(self, q, k, v, out=None):  # type: ignore[no-untyped-def]
         import torch
 
         from repercep_runtime_b200 import ops

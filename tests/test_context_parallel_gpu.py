@@ -81,7 +81,7 @@ def _nccl_worker(rank: int, world: int, port: int, S: int) -> None:
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        q, k, v = (gen_bf16((1, 4, S, 128), "n05", 80 + i).cuda() for i in range(3))
+        q, k, v = (gen_bf16((1, 12, S, 128), "n05", 80 + i).cuda() for i in range(3))
         cp = ContextParallelAttention(S, rank, world, all_gather=nccl_all_gather())
         sh = cp.shard
         sl = slice(sh.start, sh.start + sh.rows)
@@ -89,6 +89,10 @@ def _nccl_worker(rank: int, world: int, port: int, S: int) -> None:
         ref = _single(q, k, v)[:, :, sl]
         torch.cuda.synchronize()
         assert torch.equal(out, ref), f"rank {rank}"
+        # host shards: chunks streamed through the device, same bits
+        host = [t[:, :, sl].contiguous().cpu().pin_memory() for t in (q, k, v)]
+        out_h = cp(*host)
+        assert out_h.device.type == "cpu" and torch.equal(out_h, ref.cpu()), f"rank {rank} (host)"
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -98,4 +102,5 @@ def _nccl_worker(rank: int, world: int, port: int, S: int) -> None:
 def test_context_parallel_over_nccl():
     import torch.multiprocessing as mp
 
-    mp.spawn(_nccl_worker, args=(2, _free_port(), 2000), nprocs=2, join=True)
+    # 32768 tokens: 16384-row shards, 64 CTAs per slice -> the host path cuts 4 chunks of 3 slices
+    mp.spawn(_nccl_worker, args=(2, _free_port(), 32768), nprocs=2, join=True)
