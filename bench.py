@@ -484,8 +484,10 @@ def side_measurements(runner: Runner, dev, stream, peaks: dict) -> dict:  # type
             rows[name] = {"ms": ms, "tflops": runner.rank_flops / (ms / 1e3) / 1e12}
         except Exception as e:  # backend not available for this shape / build
             rows[name] = {"unavailable": f"{type(e).__name__}: {str(e)[:120]}"}
-    rows["reference_fp8_triton"] = {"unavailable": "the reference's Triton source does not travel to "
-                                    "the GPU box; its CPU path is the --impl reference arm"}
+    rows["reference_fp8_triton"] = {"unavailable": "the reference's Triton FP8 kernel lives in its "
+                                    "kernels/triton_kernels tree, outside its installable package "
+                                    "(src/repercep), so nothing of it reaches the GPU box; its CPU "
+                                    "path is the --impl reference arm"}
     out["gpu_comparison"] = rows
     torch.cuda.synchronize(dev)
     return out
