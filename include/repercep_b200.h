@@ -26,6 +26,10 @@
  *                             context parallelism, attention/diffusers_backend.py:199-212)
  *   rp_attn_fp8_prefix_decode <- (no reference kernel: the reference expands the
  *                             prompt per candidate, scripts/run_vla_openvla_gpu.py:174-186)
+ *   rp_fp8_gemm            <- fp8_gemm_launch, kernels/hip/fp8_attn/fp8_gemm.hip:162-179
+ *                             (bound by fp8_gemm, kernels/hip/fp8_attn/binding.cpp:24-61)
+ *   rp_fp8_gemm_ex, rp_quant_fp8_rows <- (no reference kernel: FP8 DiT linears are the
+ *                             reference's planned use of that GEMM, docs/OPTIMIZATION.md:161-162)
  */
 #ifndef REPERCEP_B200_H_
 #define REPERCEP_B200_H_
@@ -37,7 +41,7 @@
 extern "C" {
 #endif
 
-#define RP_ABI_VERSION 2
+#define RP_ABI_VERSION 3
 
 typedef enum rp_status {
   RP_OK = 0,
@@ -185,6 +189,52 @@ int rp_attn_fp8_prefix_decode(const void* q8, const void* kp8, const void* vp8,
                               const float* vxs, int C, int T, int P, int H, int D,
                               float sm_scale, int p_mode, void* out,
                               const int64_t* out_strides, void* stream);
+
+/* ------------------------------------------------------------ FP8 GEMM
+ * C = A @ B on the tensor cores with e4m3 operands and an fp32 accumulator.
+ *
+ * rp_fp8_gemm is the reference's fp8_gemm_launch: A (M, K) and B (K, N)
+ * row-major e4m3, C (M, N) row-major bf16, all contiguous,
+ *   C = bf16_rne(acc * (a_scale * b_scale)).
+ * e4m3 is the OCP e4m3fn encoding (torch.float8_e4m3fn) that B200 computes
+ * in; the reference's gfx942 operands are e4m3fnuz.  The TMA unit needs
+ * 16-byte row pitches: K and N must be multiples of 16 here
+ * (rp_fp8_gemm_ex takes padded pitches). */
+typedef enum rp_b_layout {
+  RP_B_KN = 0, /* B is (K, N), N contiguous (the reference's layout)       */
+  RP_B_NK = 1  /* B is (N, K), K contiguous (an nn.Linear weight)           */
+} rp_b_layout;
+
+int rp_fp8_gemm(const void* a, const void* b, void* c, float a_scale, float b_scale, int M,
+                int N, int K, void* stream);
+
+/* General form, for FP8 linears:
+ *   C[m, n] = out( acc[m, n] * (sa_m * sb_n) + bias[n] )
+ *   a      (M, K) e4m3, row m at a + m * lda bytes (lda % 16 == 0)
+ *   b      RP_B_KN: (K, N), row k at b + k * ldb bytes; RP_B_NK: (N, K),
+ *          row n at b + n * ldb bytes (ldb % 16 == 0)
+ *   sa_m   = sa[m * sa_stride] (sa_stride 0: one device scalar), or a_scale
+ *            when sa is NULL; sb_n likewise with sb / sb_stride / b_scale
+ *   bias   NULL or (N,) in the output dtype
+ *   c      (M, N) bf16 or fp16 (out_dtype, an rp_dtype), row m at
+ *          c + m * ldc elements
+ * The product of the two scales is formed first, then acc times it, then the
+ * bias is added (fp32, round to nearest) and the sum rounded to the output
+ * dtype.  K may be any size (the tensor map zero-fills past K). */
+int rp_fp8_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, int b_layout,
+                   const float* sa, int64_t sa_stride, float a_scale, const float* sb,
+                   int64_t sb_stride, float b_scale, const void* bias, void* c, int64_t ldc,
+                   int out_dtype, int M, int N, int K, void* stream);
+
+/* Row-wise e4m3 quantizer for linear operands: x (rows, cols) bf16 or fp16
+ * (in_dtype), row r at x + r * ldx elements (16-byte aligned rows, cols % 8
+ * == 0), to out (rows, cols) e4m3 with row pitch ldo bytes (ldo % 8 == 0)
+ * and scales[r] (fp32 dequant multiplier).  Each row is one scale group of
+ * rp_quant_fp8_e4m3's recipe (amax, 1e-6 floor, amax/425.6 rounded to the
+ * input format, reciprocal, clamp, e4m3 RNE): per-token activation scales
+ * for the A operand, per-output-channel weight scales for an RP_B_NK B. */
+int rp_quant_fp8_rows(const void* x, int64_t ldx, int in_dtype, int rows, int cols, void* out,
+                      int64_t ldo, float* scales, void* stream);
 
 #ifdef __cplusplus
 }

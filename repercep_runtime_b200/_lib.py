@@ -21,6 +21,8 @@ RP_P_E4M3 = 0
 RP_P_E4M3_HILO = 1
 RP_DTYPE_BF16 = 0
 RP_DTYPE_F16 = 1
+RP_B_KN = 0
+RP_B_NK = 1
 
 STATUS_NAMES = {
     -1: "RP_ERR_INVALID",
@@ -125,9 +127,41 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         + [_c_int] * 5
         + [_c_float, _c_int, _c_void_p, _c_i64_p, _c_void_p],
     ),
+    "rp_fp8_gemm": (
+        _c_int,
+        [_c_void_p, _c_void_p, _c_void_p, _c_float, _c_float, _c_int, _c_int, _c_int, _c_void_p],
+    ),
+    "rp_fp8_gemm_ex": (
+        _c_int,
+        [
+            _c_void_p,
+            ctypes.c_int64,
+            _c_void_p,
+            ctypes.c_int64,
+            _c_int,
+            _c_void_p,
+            ctypes.c_int64,
+            _c_float,
+            _c_void_p,
+            ctypes.c_int64,
+            _c_float,
+            _c_void_p,
+            _c_void_p,
+            ctypes.c_int64,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_void_p,
+        ],
+    ),
+    "rp_quant_fp8_rows": (
+        _c_int,
+        [_c_void_p, ctypes.c_int64, _c_int, _c_int, _c_int, _c_void_p, ctypes.c_int64, _c_void_p, _c_void_p],
+    ),
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

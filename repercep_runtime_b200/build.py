@@ -22,7 +22,7 @@ INCLUDE = REPO_DIR / "include"
 LIB_NAME = "librepercep_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ("capi.cu", "quantize.cu", "quantize_noalloc.cu", "attention.cu")
+SOURCES = ("capi.cu", "quantize.cu", "quantize_noalloc.cu", "attention.cu", "gemm.cu")
 
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 

@@ -133,6 +133,16 @@ int make_out_map(CUtensorMap* m, void* base, int B, int H, int S, int64_t sB, in
                   plain ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// e4m3 matrix of `rows` rows of `cols` bytes, `ld` bytes apart: boxes of 128
+// bytes x box_rows rows in the 128-byte swizzle (zero fill past the edges).
+int make_mat8_map(CUtensorMap* m, const void* base, int64_t cols, int64_t rows, int64_t ld,
+                  uint32_t box_rows, const char* what) {
+  const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)rows, 1, 1};
+  uint64_t strides[3] = {(uint64_t)ld, (uint64_t)ld * rows, (uint64_t)ld * rows};
+  const uint32_t box[4] = {128, box_rows, 1, 1};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, dims, strides, box, what);
+}
+
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
 int ceil_div(int a, int b) { return (a + b - 1) / b; }
@@ -499,6 +509,105 @@ int rp_attn_fp8_prefix_decode(const void* q8, const void* kp8, const void* vp8,
   p.causal = 0;
   cudaError_t e = rp::launch_attention(m, p, 1, H, 1, p_mode, 1, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return RP_OK;
+}
+
+
+int rp_fp8_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, int b_layout,
+                   const float* sa, int64_t sa_stride, float a_scale, const float* sb,
+                   int64_t sb_stride, float b_scale, const void* bias, void* c, int64_t ldc,
+                   int out_dtype, int M, int N, int K, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(RP_ERR_INVALID, "M, N, K must be non-negative");
+  if (b_layout != RP_B_KN && b_layout != RP_B_NK)
+    return fail(RP_ERR_INVALID, "unknown b_layout %d", b_layout);
+  if (out_dtype != RP_DTYPE_BF16 && out_dtype != RP_DTYPE_F16)
+    return fail(RP_ERR_UNSUPPORTED, "output dtype %d is neither bf16 nor fp16", out_dtype);
+  if (M == 0 || N == 0) return RP_OK;
+  if (!c || (K > 0 && (!a || !b)))
+    return fail(RP_ERR_INVALID, "a, b and c must be non-null");
+  const int64_t b_cols = (b_layout == RP_B_NK) ? K : N;
+  if (lda < K || ldb < b_cols || ldc < N)
+    return fail(RP_ERR_INVALID, "row pitches lda=%lld ldb=%lld ldc=%lld are shorter than the rows",
+                (long long)lda, (long long)ldb, (long long)ldc);
+  if (lda % 16 != 0 || ldb % 16 != 0)
+    return fail(RP_ERR_ALIGN, "e4m3 row pitches must be multiples of 16 bytes (lda=%lld ldb=%lld)",
+                (long long)lda, (long long)ldb);
+  if ((sa && sa_stride < 0) || (sb && sb_stride < 0))
+    return fail(RP_ERR_INVALID, "scale strides must be non-negative");
+  int* status = nullptr;
+  int rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+
+  // K = 0: no K blocks, the operands are never read and need no maps.
+  CUtensorMap ma{}, mb{};
+  if (K > 0) {
+    if ((rc = make_mat8_map(&ma, a, K, M, lda, rp::gemm_tile_m(), "a")) != RP_OK) return rc;
+    if (b_layout == RP_B_NK)
+      rc = make_mat8_map(&mb, b, K, N, ldb, rp::gemm_tile_n(), "b");
+    else
+      rc = make_mat8_map(&mb, b, N, K, ldb, 128, "b");
+    if (rc != RP_OK) return rc;
+  }
+
+  rp::GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.group_m = 0;
+  p.sa = sa;
+  p.sa_stride = sa_stride;
+  p.a_scale = a_scale;
+  p.sb = sb;
+  p.sb_stride = sb_stride;
+  p.b_scale = b_scale;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.C = c;
+  p.ldc = ldc;
+  p.vec_store = (aligned16(c) && (ldc * 2) % 16 == 0) ? 1 : 0;
+  p.status = status;
+  cudaError_t e = rp::launch_fp8_gemm(ma, mb, p, b_layout == RP_B_NK, out_dtype == RP_DTYPE_F16,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 gemm launch");
+  return RP_OK;
+}
+
+int rp_fp8_gemm(const void* a, const void* b, void* c, float a_scale, float b_scale, int M,
+                int N, int K, void* stream) {
+  if (K % 16 != 0 || N % 16 != 0)
+    return fail(RP_ERR_ALIGN,
+                "contiguous e4m3 rows need K and N to be multiples of 16 (K=%d N=%d); "
+                "rp_fp8_gemm_ex takes padded pitches", K, N);
+  return rp_fp8_gemm_ex(a, K, b, N, RP_B_KN, nullptr, 0, a_scale, nullptr, 0, b_scale, nullptr,
+                        c, N, RP_DTYPE_BF16, M, N, K, stream);
+}
+
+int rp_quant_fp8_rows(const void* x, int64_t ldx, int in_dtype, int rows, int cols, void* out,
+                      int64_t ldo, float* scales, void* stream) {
+  if (rows < 0 || cols < 0) return fail(RP_ERR_INVALID, "rows and cols must be non-negative");
+  if (in_dtype != RP_DTYPE_BF16 && in_dtype != RP_DTYPE_F16)
+    return fail(RP_ERR_UNSUPPORTED, "input dtype %d is neither bf16 nor fp16", in_dtype);
+  if (rows == 0) return RP_OK;
+  if (!x || !out || !scales) return fail(RP_ERR_INVALID, "x, out and scales must be non-null");
+  if (cols % 8 != 0) return fail(RP_ERR_UNSUPPORTED, "cols (%d) must be a multiple of 8", cols);
+  if (ldx < cols || ldo < cols) return fail(RP_ERR_INVALID, "row pitches are shorter than the rows");
+  if (!aligned16(x) || ldx % 8 != 0)
+    return fail(RP_ERR_ALIGN, "x rows must start on 16-byte boundaries");
+  if (reinterpret_cast<uintptr_t>(out) % 8 != 0 || ldo % 8 != 0)
+    return fail(RP_ERR_ALIGN, "out rows must start on 8-byte boundaries");
+  int* status = nullptr;
+  int rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+  rp::QuantRowsArgs q{};
+  q.x = static_cast<const uint16_t*>(x);
+  q.ldx = ldx;
+  q.rows = rows;
+  q.cols = cols;
+  q.in_f16 = (in_dtype == RP_DTYPE_F16) ? 1 : 0;
+  q.out = static_cast<uint8_t*>(out);
+  q.ldo = ldo;
+  q.scales = scales;
+  cudaError_t e = rp::launch_quant_rows(q, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "row quantize launch");
   return RP_OK;
 }
 

@@ -36,6 +36,44 @@ struct QuantArgs {
 cudaError_t launch_quant_block(const QuantArgs& a, int njobs, cudaStream_t st);
 cudaError_t launch_quant_bh(const QuantArgs& a, int njobs, cudaStream_t st);
 
+// Row-wise quantizer of a linear operand: one scale per row of (rows, cols).
+struct QuantRowsArgs {
+  const uint16_t* x;   // bf16 / fp16, row r at x + r * ldx (elements; 16-byte aligned rows)
+  int64_t ldx;
+  int rows, cols;      // cols a multiple of 8
+  int in_f16;
+  uint8_t* out;        // e4m3, row r at out + r * ldo (bytes)
+  int64_t ldo;
+  float* scales;       // (rows,)
+};
+cudaError_t launch_quant_rows(const QuantRowsArgs& a, cudaStream_t st);
+
+// --------------------------------------------------------------- fp8 GEMM
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, tiles, n_kb;  // filled by launch_fp8_gemm
+  int group_m;                        // row tiles per raster group (0: default)
+  // Dequant scales: row m uses sa[m * sa_stride] (sa_stride 0: one device
+  // scalar) or a_scale when sa is null; columns likewise with sb / b_scale.
+  const float* sa;
+  int64_t sa_stride;
+  float a_scale;
+  const float* sb;
+  int64_t sb_stride;
+  float b_scale;
+  const uint16_t* bias;  // (N,) in the output dtype, or null
+  void* C;               // 16-bit output, row m at C + m * ldc (elements)
+  int64_t ldc;
+  int vec_store;         // C and ldc allow 16-byte stores
+  int* status;           // device status word (0 = ok)
+};
+
+// b_kmajor: B is (N, K) with K contiguous; otherwise (K, N) with N contiguous.
+cudaError_t launch_fp8_gemm(const CUtensorMap& a, const CUtensorMap& b, GemmParams p,
+                            bool b_kmajor, bool out_f16, cudaStream_t st);
+int gemm_tile_m();
+int gemm_tile_n();
+
 // ------------------------------------------------------------ attention
 struct AttnKernelParams {
   int H;                 // heads (bh -> (b, h) for the output map)

@@ -218,9 +218,41 @@ __global__ void __launch_bounds__(kQuantThreads) quant_bh_kernel(const QuantArgs
   t.store(j, bh, a.S, a.out_ld, s0, rows, __frcp_rn(sc));
 }
 
+// Row-wise scales for the linear operands: one scale group per row of an
+// (rows, cols) matrix (a token of the activations, an output channel of a
+// weight), with the steps above.  One warp per row; the second pass re-reads
+// the row from L1/L2.
+template <bool F16>
+__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantRowsArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (kQuantThreads / 32) + warp;
+  if (row >= a.rows) return;
+  const uint4* x = reinterpret_cast<const uint4*>(a.x + row * a.ldx);
+  const int nv = a.cols / 8;
+  uint32_t m = 0;
+  for (int i = lane; i < nv; i += 32) m = max(m, absmax8(__ldg(x + i)));
+  m = __reduce_max_sync(0xffffffffu, m);
+  const float sc = scale_from_amax_bits<F16>(m);
+  if (lane == 0) a.scales[row] = sc;
+  const float qm = __frcp_rn(sc);
+  uint2* o = reinterpret_cast<uint2*>(a.out + row * a.ldo);
+  for (int i = lane; i < nv; i += 32) __stcs(o + i, quant8<F16>(__ldg(x + i), qm));
+}
+
 }  // namespace
 
-#define RP_DISPATCH_DF(KERNEL, F16)                                                  \
+cudaError_t launch_quant_rows(const QuantRowsArgs& a, cudaStream_t st) {
+  constexpr int kRowsPerCta = kQuantThreads / 32;
+  const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
+  if (grid > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  if (a.in_f16)
+    quant_rows_kernel<true><<<static_cast<unsigned>(grid), kQuantThreads, 0, st>>>(a);
+  else
+    quant_rows_kernel<false><<<static_cast<unsigned>(grid), kQuantThreads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+#define RP_DISPATCH_DF(KERNEL, F16)                                               \
   switch (a.D) {                                                                     \
     case 32: KERNEL<32, F16><<<grid, kQuantThreads, 0, st>>>(a); break;             \
     case 64: KERNEL<64, F16><<<grid, kQuantThreads, 0, st>>>(a); break;             \

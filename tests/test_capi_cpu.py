@@ -104,6 +104,31 @@ def test_extended_entry_points_check_dtype_rows_and_head_dim(lib):
     assert rc == -2 and b"_ex" in lib.rp_last_error()
 
 
+def test_gemm_entry_points_check_shapes_and_pitches(lib):
+    dummy = 1 << 20
+    # the reference-compatible entry point needs 16-byte rows (K, N multiples of 16)
+    assert lib.rp_fp8_gemm(dummy, dummy, dummy, 1.0, 1.0, 16, 16, 40, None) == -3
+    assert b"multiples of 16" in lib.rp_last_error()
+
+    def ex(lda, ldb, layout, out_dtype=0, M=16, N=16, K=32, a=dummy):  # type: ignore[no-untyped-def]
+        return lib.rp_fp8_gemm_ex(a, lda, dummy, ldb, layout, None, 0, 1.0, None, 0, 1.0, None,
+                                  dummy, N, out_dtype, M, N, K, None)
+
+    assert ex(32, 32, 2) == -1 and b"b_layout" in lib.rp_last_error()
+    assert ex(32, 32, 0, out_dtype=4) == -2 and b"dtype" in lib.rp_last_error()
+    assert ex(16, 32, 1) == -1 and b"shorter" in lib.rp_last_error()      # lda < K
+    assert ex(40, 48, 1) == -3 and b"16 bytes" in lib.rp_last_error()     # lda % 16
+    assert ex(32, 32, 0, a=None) == -1 and b"non-null" in lib.rp_last_error()
+    assert ex(32, 32, 0, M=-1) == -1
+    assert ex(32, 32, 0, M=0) == 0  # empty output: nothing to launch
+    # row quantizer
+    assert lib.rp_quant_fp8_rows(dummy, 16, 0, 4, 12, dummy, 16, dummy, None) == -2  # cols % 8
+    assert lib.rp_quant_fp8_rows(dummy, 16, 3, 4, 16, dummy, 16, dummy, None) == -2  # dtype
+    assert lib.rp_quant_fp8_rows(dummy + 8, 16, 0, 4, 16, dummy, 16, dummy, None) == -3
+    assert lib.rp_quant_fp8_rows(dummy, 16, 0, 4, 16, dummy + 4, 16, dummy, None) == -3
+    assert lib.rp_quant_fp8_rows(dummy, 16, 0, 0, 16, dummy, 16, dummy, None) == 0
+
+
 def test_rescale_threshold_default(lib, monkeypatch):
     # read once per process from REPERCEP_B200_RESCALE_TAU; the default is 1
     import os
