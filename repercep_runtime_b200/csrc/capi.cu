@@ -541,11 +541,11 @@ int rp_fp8_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, int b
   // K = 0: no K blocks, the operands are never read and need no maps.
   CUtensorMap ma{}, mb{};
   if (K > 0) {
-    if ((rc = make_mat8_map(&ma, a, K, M, lda, rp::gemm_tile_m(), "a")) != RP_OK) return rc;
+    if ((rc = make_mat8_map(&ma, a, K, M, lda, 128, "a")) != RP_OK) return rc;
     if (b_layout == RP_B_NK)
-      rc = make_mat8_map(&mb, b, K, N, ldb, rp::gemm_tile_n(), "b");
+      rc = make_mat8_map(&mb, b, K, N, ldb, rp::gemm_b_box_rows(true), "b");
     else
-      rc = make_mat8_map(&mb, b, N, K, ldb, 128, "b");
+      rc = make_mat8_map(&mb, b, N, K, ldb, rp::gemm_b_box_rows(false), "b");
     if (rc != RP_OK) return rc;
   }
 

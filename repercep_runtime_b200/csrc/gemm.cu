@@ -11,19 +11,27 @@
 // the two scales are multiplied first, then the accumulator, then the bias is
 // added (three fp32 roundings) and the sum is rounded to bf16 / fp16 (RNE).
 //
-// Kernel: persistent, one CTA per SM, 128 x 256 output tiles in a grouped
-// raster (group_m row tiles share each column tile while it is hot in L2).
-//   warp 0     TMA producer: per 128-byte K block an A box (128 rows) and a B
-//              box (256 rows, K-major) or two (128 K rows x 128 N bytes,
-//              N-major), 128-byte swizzle, into a 4-stage ring of 48 KB;
-//   warp 1     MMA issuer (one thread): four tcgen05.mma kind::f8f6f4 M128
-//              N256 K32 per stage into one of two TMEM accumulators (2 x 256
-//              columns), so tile t+1's MMAs run while the epilogue drains t;
-//   warps 2-9  epilogue: two warps per TMEM lane quarter, one per 128-column
-//              half; each stages its columns' scales and bias in its own slice
-//              of shared memory before the accumulator is ready, then
-//              tcgen05.ld 2 x 32 columns in flight, scale, bias, round,
+// Kernel: persistent, 256 x 256 output tiles in a grouped raster (group_m
+// row tiles share each column tile while it is hot in L2), one tile per pair
+// of CTAs on the two SMs of a TPC (a cluster of 2):
+//   warp 0     TMA producer: per 128-byte K block this CTA's 128 A rows and
+//              128 B rows (K-major) or columns (N-major), 128-byte swizzle,
+//              into a 6-stage ring of 32 KB; the bytes of both CTAs complete
+//              on rank 0's barrier;
+//   warp 1     MMA issuer (one thread of rank 0): four tcgen05.mma
+//              cta_group::2 kind::f8f6f4 M256 N256 K32 per stage, reading
+//              both CTAs' shared memory, into one of two accumulators (2 x
+//              256 TMEM columns in each CTA: its 128 rows), so tile t+1's MMAs
+//              run while the epilogue drains t;
+//   warps 2-9  epilogue (both CTAs): two warps per TMEM lane quarter, one per
+//              128-column half; each stages its columns' scales and bias in
+//              its own slice of shared memory before the accumulator is ready,
+//              then tcgen05.ld 2 x 32 columns in flight, scale, bias, round,
 //              16-byte global stores (each thread owns one row).
+// Splitting B across the pair halves what each SM pulls from L2 per MMA
+// (32 KB instead of 48 KB per 128-deep K block).  REPERCEP_B200_GEMM_PAIR=0
+// selects the single-CTA form: 128 x 256 tiles, one CTA per SM, a 4-stage
+// ring of 48 KB (A 128 rows, B 256).
 // K, M and N tails need no special case: the TMA unit fills out-of-range box
 // elements with zeros (they add nothing to acc) and the epilogue masks rows
 // and columns past M and N.
@@ -31,6 +39,7 @@
 #include <cuda_fp16.h>
 
 #include <atomic>
+#include <cstdlib>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -39,26 +48,33 @@ namespace rp {
 
 namespace {
 
-constexpr int kBM = 128;  // output rows per tile (TMEM lanes)
-constexpr int kBN = 256;  // output columns per tile (TMEM columns per accumulator)
 constexpr int kBK = 128;  // K bytes per stage (one 128-byte swizzle row)
-constexpr int kStages = 4;
-constexpr int kABytes = kBM * kBK;                 // 16 KB
-constexpr int kBBytes = kBN * kBK;                 // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;     // 48 KB
-constexpr int kHalfB = kBBytes / 2;                // one 128-column N-major box
-constexpr int kTmaWarp = 0, kMmaWarp = 1;          // warps 2..9: epilogue
+constexpr int kCtaRows = 128;  // A rows (TMEM lanes) per CTA
+constexpr int kTileN = 256;    // output columns per tile (TMEM columns per accumulator)
+constexpr int kABytes = kCtaRows * kBK;  // 16 KB
+constexpr int kTmaWarp = 0, kMmaWarp = 1;  // warps 2..9: epilogue
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kEpiCols = kBN / 2;                  // columns per epilogue warp
-constexpr int kTmemCols = 2 * kBN;                 // two accumulators
+constexpr int kEpiCols = kTileN / 2;       // columns per epilogue warp
+constexpr int kTmemCols = 2 * kTileN;      // two accumulators
 // Per epilogue warp: kEpiCols column scales then kEpiCols bias values (fp32).
-constexpr int kOffCol = kStages * kStageBytes;
 constexpr int kColBytes = kEpiWarps * 2 * kEpiCols * 4;
-constexpr int kOffBar = kOffCol + kColBytes;
-constexpr int kNumBars = 2 * kStages + 2 + 2 + 1;  // full, empty, acc_full, acc_empty, fin
-constexpr int kSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+template <bool PAIR>
+struct GCfg {
+  static constexpr int kTileM = PAIR ? 2 * kCtaRows : kCtaRows;  // output rows per tile
+  static constexpr int kBRows = PAIR ? kTileN / 2 : kTileN;      // B rows (N) per CTA
+  static constexpr int kBBytes = kBRows * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;           // 32 / 48 KB
+  static constexpr int kStages = PAIR ? 6 : 4;
+  static constexpr int kOffCol = kStages * kStageBytes;
+  static constexpr int kOffBar = kOffCol + kColBytes;
+  static constexpr int kNumBars = 2 * kStages + 2 + 2 + 1;  // full, empty, acc_full, acc_empty, fin
+  static constexpr int kSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
+  // acc_empty arrivals: every epilogue warp of the pair
+  static constexpr int kAccEmptyCount = (PAIR ? 2 : 1) * kEpiWarps;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
 
 enum : int {
   kErrGemmFull = 0x201,
@@ -77,7 +93,9 @@ struct GemmBars {
   uint32_t* tmem_slot;
 };
 
+template <bool PAIR>
 __device__ __forceinline__ GemmBars carve_gemm_bars(uint8_t* s) {
+  constexpr int kStages = GCfg<PAIR>::kStages, kNumBars = GCfg<PAIR>::kNumBars;
   uint64_t* b = reinterpret_cast<uint64_t*>(s);
   GemmBars r;
   r.full = b;
@@ -111,81 +129,139 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmParams& p, int t) {
   return {first + r % rows, r / rows};
 }
 
-template <bool BKM>
+// Tile loop position of this CTA (PAIR: of its pair).
+template <bool PAIR>
+__device__ __forceinline__ int tile_unit() {
+  return PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+}
+template <bool PAIR>
+__device__ __forceinline__ int tile_units() {
+  return PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+}
+
+template <bool PAIR>
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const GemmBars& b,
+                                         int* status, int code) {
+  return PAIR ? mbar_wait_cluster(bar, parity, b.abort_flag, status, code)
+              : mbar_wait(bar, parity, b.abort_flag, status, code);
+}
+
+template <bool PAIR, bool BKM>
 __device__ void gemm_producer(const CUtensorMap* ta, const CUtensorMap* tb, const GemmParams& p,
-                              const GemmBars& bar, uint8_t* smem) {
+                              const GemmBars& bar, uint8_t* smem, uint32_t rank) {
+  using C = GCfg<PAIR>;
   int g = 0;
   bool ok = true;
-  for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+  for (int t = tile_unit<PAIR>(); ok && t < p.tiles; t += tile_units<PAIR>()) {
     const TileCoord c = tile_coord(p, t);
+    const int m0 = c.m * C::kTileM + static_cast<int>(rank) * kCtaRows;
+    const int n0 = c.n * kTileN + static_cast<int>(rank) * C::kBRows;
     for (int kb = 0; kb < p.n_kb; ++kb, ++g) {
-      const int s = g % kStages;
-      if (!mbar_wait(bar.empty + s, ((g / kStages) & 1) ^ 1, bar.abort_flag, p.status,
-                     kErrGemmEmpty)) {
+      const int s = g % C::kStages;
+      if (!wait_bar<PAIR>(bar.empty + s, ((g / C::kStages) & 1) ^ 1, bar, p.status,
+                          kErrGemmEmpty)) {
         ok = false;
         break;
       }
-      uint8_t* sa = smem + s * kStageBytes;
+      uint8_t* sa = smem + s * C::kStageBytes;
       uint8_t* sb = sa + kABytes;
-      mbar_arrive_expect_tx(bar.full + s, kStageBytes);
-      tma_load_4d(sa, ta, bar.full + s, kb * kBK, c.m * kBM, 0, 0);
-      if constexpr (BKM) {
-        tma_load_4d(sb, tb, bar.full + s, kb * kBK, c.n * kBN, 0, 0);
+      if constexpr (PAIR) {
+        // Both CTAs' bytes complete on rank 0's barrier, which rank 0 arms.
+        if (rank == 0) mbar_arrive_expect_tx(bar.full + s, 2 * C::kStageBytes);
+        const uint32_t fb = mapa_shared(smem_u32(bar.full + s), 0);
+        tma_load_4d_pair(sa, ta, fb, kb * kBK, m0, 0, 0);
+        if constexpr (BKM)
+          tma_load_4d_pair(sb, tb, fb, kb * kBK, n0, 0, 0);
+        else
+          tma_load_4d_pair(sb, tb, fb, n0, kb * kBK, 0, 0);
       } else {
-        tma_load_4d(sb, tb, bar.full + s, c.n * kBN, kb * kBK, 0, 0);
-        tma_load_4d(sb + kHalfB, tb, bar.full + s, c.n * kBN + 128, kb * kBK, 0, 0);
+        mbar_arrive_expect_tx(bar.full + s, C::kStageBytes);
+        tma_load_4d(sa, ta, bar.full + s, kb * kBK, m0, 0, 0);
+        if constexpr (BKM) {
+          tma_load_4d(sb, tb, bar.full + s, kb * kBK, n0, 0, 0);
+        } else {
+          tma_load_4d(sb, tb, bar.full + s, n0, kb * kBK, 0, 0);
+          tma_load_4d(sb + C::kBBytes / 2, tb, bar.full + s, n0 + 128, kb * kBK, 0, 0);
+        }
       }
     }
   }
   if (!ok) {
     // Loads still in flight write this CTA's shared memory: let them land.
-    for (int s = 0; s < kStages; ++s) {
-      if (s >= g) break;
-      const int last = g - 1 - ((g - 1 - s) % kStages);  // last fill of stage s
-      drain(bar.full + s, (last / kStages) & 1);
+    if (PAIR && rank != 0) {
+      // (their bytes complete on rank 0's barriers): a fixed grace period
+      const long long t0 = clock64();
+      while (clock64() - t0 < 2000000) {
+      }
+    } else {
+      for (int s = 0; s < C::kStages; ++s) {
+        if (s >= g) break;
+        const int last = g - 1 - ((g - 1 - s) % C::kStages);  // last fill of stage s
+        drain(bar.full + s, (last / C::kStages) & 1);
+      }
     }
   }
 }
 
-template <bool BKM>
+// Signals `bar` (same offset in both CTAs for PAIR) when the MMAs issued so
+// far are done.
+template <bool PAIR>
+__device__ __forceinline__ void commit_both(uint64_t* bar) {
+  if constexpr (PAIR) {
+    mma_commit_pair_to(bar, 0x3);
+  } else {
+    mma_commit(bar);
+  }
+}
+
+template <bool PAIR, bool BKM>
 __device__ void gemm_mma(const GemmParams& p, const GemmBars& bar, uint32_t sbase,
                          uint32_t tmem) {
-  constexpr uint32_t idesc = make_idesc_e4m3(kBM, kBN, 0, BKM ? 0 : 1);
+  using C = GCfg<PAIR>;
+  constexpr uint32_t idesc = make_idesc_e4m3(C::kTileM, kTileN, 0, BKM ? 0 : 1);
   int g = 0, it = 0;
   bool ok = true;
-  for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++it) {
+  for (int t = tile_unit<PAIR>(); ok && t < p.tiles; t += tile_units<PAIR>(), ++it) {
     const int buf = it & 1;
-    if (!mbar_wait(bar.acc_empty + buf, ((it >> 1) & 1) ^ 1, bar.abort_flag, p.status,
-                   kErrGemmAccEmpty)) {
+    if (!wait_bar<PAIR>(bar.acc_empty + buf, ((it >> 1) & 1) ^ 1, bar, p.status,
+                        kErrGemmAccEmpty)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    const uint32_t d = tmem + buf * kBN;
+    const uint32_t d = tmem + buf * kTileN;
     for (int kb = 0; kb < p.n_kb; ++kb, ++g) {
-      const int s = g % kStages;
-      if (!mbar_wait(bar.full + s, (g / kStages) & 1, bar.abort_flag, p.status, kErrGemmFull)) {
+      const int s = g % C::kStages;
+      if (!wait_bar<PAIR>(bar.full + s, (g / C::kStages) & 1, bar, p.status, kErrGemmFull)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t a_addr = sbase + s * kStageBytes;
+      const uint32_t a_addr = sbase + s * C::kStageBytes;
       const uint64_t ad = make_sw128_desc(a_addr, 16, 1024);
-      // K-major B: 8-row groups 1024 B apart, K step 32 B.  N-major B: the
-      // two 128-column boxes kHalfB apart (LBO), 8-K-row groups 1024 B apart
-      // (SBO), K step 32 rows = 4096 B.
+      // K-major B: 8-row groups 1024 B apart, K step 32 B.  N-major B: 128-
+      // column boxes C::kBBytes / 2 apart (LBO; one box per CTA when PAIR),
+      // 8-K-row groups 1024 B apart (SBO), K step 32 rows = 4096 B.
       const uint64_t bd = BKM ? make_sw128_desc(a_addr + kABytes, 16, 1024)
-                              : make_sw128_desc(a_addr + kABytes, kHalfB, 1024);
+                              : make_sw128_desc(a_addr + kABytes, C::kBBytes / 2, 1024);
 #pragma unroll
-      for (int k = 0; k < kBK / 32; ++k)
-        mma_f8(d, ad + 2 * k, bd + (BKM ? 2 * k : 256 * k), idesc, (kb | k) ? 1u : 0u);
-      mma_commit(bar.empty + s);
+      for (int k = 0; k < kBK / 32; ++k) {
+        const uint64_t bk = bd + (BKM ? 2 * k : 256 * k);
+        if constexpr (PAIR)
+          mma_f8_pair(d, ad + 2 * k, bk, idesc, (kb | k) ? 1u : 0u);
+        else
+          mma_f8(d, ad + 2 * k, bk, idesc, (kb | k) ? 1u : 0u);
+      }
+      commit_both<PAIR>(bar.empty + s);
     }
     if (!ok) break;
-    mma_commit(bar.acc_full + buf);
+    commit_both<PAIR>(bar.acc_full + buf);
   }
   // Everything this thread issued must finish before TMEM is released.
-  mma_commit(bar.fin);
+  if constexpr (PAIR)
+    mma_commit_pair(bar.fin);
+  else
+    mma_commit(bar.fin);
   drain(bar.fin, 0);
 }
 
@@ -245,9 +321,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
   }
 }
 
-template <bool F16OUT>
+template <bool PAIR, bool F16OUT>
 __device__ void gemm_epilogue(const GemmParams& p, const GemmBars& bar, uint32_t tmem,
-                              float* colbuf) {
+                              float* colbuf, uint32_t rank) {
+  using C = GCfg<PAIR>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ew = warp - 2;                // epilogue warp 0..7
   const int q = warp & 3;                 // TMEM lane quarter this warp may access
@@ -256,10 +333,10 @@ __device__ void gemm_epilogue(const GemmParams& p, const GemmBars& bar, uint32_t
   float* cs = colbuf + ew * 2 * kEpiCols;  // this warp's column scales, then bias
   float* cb = cs + kEpiCols;
   int it = 0;
-  for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++it) {
+  for (int t = tile_unit<PAIR>(); t < p.tiles; t += tile_units<PAIR>(), ++it) {
     const int buf = it & 1;
     const TileCoord c = tile_coord(p, t);
-    const int ncol0 = c.n * kBN + half * kEpiCols;
+    const int ncol0 = c.n * kTileN + half * kEpiCols;
     // Column data for this tile, fetched while the MMAs run (the previous
     // tile's reads of this slice are done: same warp, program order).
     if (col_scale || has_bias) {
@@ -273,15 +350,15 @@ __device__ void gemm_epilogue(const GemmParams& p, const GemmBars& bar, uint32_t
       }
       __syncwarp();
     }
-    const int m = c.m * kBM + q * 32 + lane;
+    const int m = c.m * C::kTileM + static_cast<int>(rank) * kCtaRows + q * 32 + lane;
     const bool row_ok = m < p.M;
     const float sa = p.sa ? (row_ok ? __ldg(p.sa + (int64_t)m * p.sa_stride) : 0.f) : p.a_scale;
     uint16_t* crow = static_cast<uint16_t*>(p.C) + (int64_t)(row_ok ? m : 0) * p.ldc;
-    if (!mbar_wait(bar.acc_full + buf, (it >> 1) & 1, bar.abort_flag, p.status, kErrGemmAccFull))
+    if (!wait_bar<PAIR>(bar.acc_full + buf, (it >> 1) & 1, bar, p.status, kErrGemmAccFull))
       return;
     tc_fence_after();
     const uint32_t taddr =
-        tmem + buf * kBN + half * kEpiCols + (static_cast<uint32_t>(q * 32) << 16);
+        tmem + buf * kTileN + half * kEpiCols + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
     for (int pr = 0; pr < kEpiCols / 64; ++pr) {
       uint32_t r0[32], r1[32];
@@ -297,7 +374,12 @@ __device__ void gemm_epilogue(const GemmParams& p, const GemmBars& bar, uint32_t
         // The accumulator may be overwritten once every warp's loads are done.
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar.acc_empty + buf);
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(mapa_shared(smem_u32(bar.acc_empty + buf), 0));
+          else
+            mbar_arrive(bar.acc_empty + buf);
+        }
       }
       const int n0 = ncol0 + pr * 64;
       if (row_ok && n0 < p.N)
@@ -310,74 +392,111 @@ __device__ void gemm_epilogue(const GemmParams& p, const GemmBars& bar, uint32_t
   }
 }
 
-template <bool BKM, bool F16OUT>
+template <bool PAIR, bool BKM, bool F16OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
+  using C = GCfg<PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  const GemmBars bar = carve_gemm_bars(smem + kOffBar);
+  const GemmBars bar = carve_gemm_bars<PAIR>(smem + C::kOffBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < C::kStages; ++s) {
       mbar_init(bar.full + s, 1);
       mbar_init(bar.empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar.acc_full + b, 1);
-      mbar_init(bar.acc_empty + b, kEpiWarps);
+      mbar_init(bar.acc_empty + b, C::kAccEmptyCount);
     }
     mbar_init(bar.fin, 1);
     *bar.abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(bar.tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(bar.tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(bar.tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (warp == kTmaWarp && lane == 0 && p.n_kb > 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
   }
   tc_fence_before();
-  __syncthreads();
+  // Both CTAs' barriers must be initialised before either signals the other's.
+  if constexpr (PAIR)
+    cluster_sync();
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *bar.tmem_slot;
 
   if (warp == kTmaWarp) {
-    if (lane == 0) gemm_producer<BKM>(&tm_a, &tm_b, p, bar, smem);
+    if (lane == 0) gemm_producer<PAIR, BKM>(&tm_a, &tm_b, p, bar, smem, rank);
   } else if (warp == kMmaWarp) {
-    if (lane == 0) gemm_mma<BKM>(p, bar, smem_u32(smem), tmem);
+    if (lane == 0 && rank == 0) gemm_mma<PAIR, BKM>(p, bar, smem_u32(smem), tmem);
   } else {
-    gemm_epilogue<F16OUT>(p, bar, tmem, reinterpret_cast<float*>(smem + kOffCol));
+    gemm_epilogue<PAIR, F16OUT>(p, bar, tmem, reinterpret_cast<float*>(smem + C::kOffCol), rank);
   }
+  __syncwarp();
 
   tc_fence_before();
-  __syncthreads();
+  // Rank 0's MMAs read rank 1's shared memory and write its TMEM: neither CTA
+  // releases either until both are done.
+  if constexpr (PAIR)
+    cluster_sync();
+  else
+    __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, kTmemCols);
+    else
+      tmem_dealloc(tmem, kTmemCols);
   }
 }
 
-template <bool BKM, bool F16OUT>
+template <bool PAIR, bool BKM, bool F16OUT>
 cudaError_t launch_gemm_variant(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
-                                int grid, cudaStream_t st) {
-  auto kern = fp8_gemm_kernel<BKM, F16OUT>;
+                                int units, cudaStream_t st) {
+  using C = GCfg<PAIR>;
+  auto kern = fp8_gemm_kernel<PAIR, BKM, F16OUT>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_release);
   }
-  kern<<<grid, kThreads, kSmemBytes, st>>>(a, b, p);
-  return cudaGetLastError();
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * units, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a, b, p);
+  } else {
+    kern<<<units, kThreads, C::kSmemBytes, st>>>(a, b, p);
+    return cudaGetLastError();
+  }
 }
 
 int sm_count() {
@@ -395,23 +514,44 @@ int sm_count() {
 
 }  // namespace
 
-int gemm_tile_m() { return kBM; }
-int gemm_tile_n() { return kBN; }
+// 2-SM pairs (1, default) or single-CTA tiles (0).  REPERCEP_B200_GEMM_PAIR
+// overrides (read once).
+bool gemm_pair_setting() {
+  static const bool v = [] {
+    const char* e = std::getenv("REPERCEP_B200_GEMM_PAIR");
+    return !(e && std::atoi(e) == 0);
+  }();
+  return v;
+}
+
+int gemm_b_box_rows(bool b_kmajor) {
+  if (!b_kmajor) return 128;  // N-major: 128 K rows x 128 N bytes per box
+  return gemm_pair_setting() ? GCfg<true>::kBRows : GCfg<false>::kBRows;
+}
+
+template <bool PAIR>
+cudaError_t launch_fp8_gemm_t(const CUtensorMap& a, const CUtensorMap& b, GemmParams p,
+                              bool b_kmajor, bool out_f16, cudaStream_t st) {
+  using C = GCfg<PAIR>;
+  p.tiles_m = (p.M + C::kTileM - 1) / C::kTileM;
+  p.tiles_n = (p.N + kTileN - 1) / kTileN;
+  p.tiles = p.tiles_m * p.tiles_n;
+  p.n_kb = (p.K + kBK - 1) / kBK;
+  if (p.group_m <= 0) p.group_m = PAIR ? 8 : 16;
+  if (p.group_m > p.tiles_m) p.group_m = p.tiles_m;
+  const int slots = PAIR ? sm_count() / 2 : sm_count();
+  const int units = p.tiles < slots ? p.tiles : slots;
+  if (b_kmajor)
+    return out_f16 ? launch_gemm_variant<PAIR, true, true>(a, b, p, units, st)
+                   : launch_gemm_variant<PAIR, true, false>(a, b, p, units, st);
+  return out_f16 ? launch_gemm_variant<PAIR, false, true>(a, b, p, units, st)
+                 : launch_gemm_variant<PAIR, false, false>(a, b, p, units, st);
+}
 
 cudaError_t launch_fp8_gemm(const CUtensorMap& a, const CUtensorMap& b, GemmParams p,
                             bool b_kmajor, bool out_f16, cudaStream_t st) {
-  p.tiles_m = (p.M + kBM - 1) / kBM;
-  p.tiles_n = (p.N + kBN - 1) / kBN;
-  p.tiles = p.tiles_m * p.tiles_n;
-  p.n_kb = (p.K + kBK - 1) / kBK;
-  if (p.group_m <= 0) p.group_m = 16;
-  if (p.group_m > p.tiles_m) p.group_m = p.tiles_m;
-  const int grid = p.tiles < sm_count() ? p.tiles : sm_count();
-  if (b_kmajor)
-    return out_f16 ? launch_gemm_variant<true, true>(a, b, p, grid, st)
-                   : launch_gemm_variant<true, false>(a, b, p, grid, st);
-  return out_f16 ? launch_gemm_variant<false, true>(a, b, p, grid, st)
-                 : launch_gemm_variant<false, false>(a, b, p, grid, st);
+  return gemm_pair_setting() ? launch_fp8_gemm_t<true>(a, b, p, b_kmajor, out_f16, st)
+                             : launch_fp8_gemm_t<false>(a, b, p, b_kmajor, out_f16, st);
 }
 
 }  // namespace rp

@@ -71,8 +71,10 @@ struct GemmParams {
 // b_kmajor: B is (N, K) with K contiguous; otherwise (K, N) with N contiguous.
 cudaError_t launch_fp8_gemm(const CUtensorMap& a, const CUtensorMap& b, GemmParams p,
                             bool b_kmajor, bool out_f16, cudaStream_t st);
-int gemm_tile_m();
-int gemm_tile_n();
+// Rows of the B box the selected kernel loads per K block (K-major B: the
+// N rows of one CTA; N-major B: 128 K rows).
+int gemm_b_box_rows(bool b_kmajor);
+bool gemm_pair_setting();
 
 // ------------------------------------------------------------ attention
 struct AttnKernelParams {

@@ -226,3 +226,23 @@ def test_dit_sized_gemm_against_torch_fp32():
     rel = ((y - ref).abs() / (ref.abs() + 1e-3)).max().item()
     cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
     assert cos > 0.99999 and rel < 2.0**-7, (cos, rel)
+
+
+def test_single_cta_kernel_passes_the_same_suite():
+    """REPERCEP_B200_GEMM_PAIR=0 selects the single-CTA kernel (128 x 256
+    tiles, no cluster); the library reads the switch once per process."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    if os.environ.get("REPERCEP_B200_GEMM_PAIR") == "0":
+        pytest.skip("already running the single-CTA kernel")
+    repo = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, REPERCEP_B200_GEMM_PAIR="0")
+    proc = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider",
+         "tests/test_gemm_gpu.py", "-k", "not single_cta"],
+        cwd=repo, env=env, capture_output=True, text=True, timeout=900,
+    )  # fmt: skip
+    assert proc.returncode == 0, proc.stdout[-4000:] + proc.stderr[-2000:]
