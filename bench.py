@@ -445,6 +445,61 @@ def _event_ms(fn, stream, n: int) -> float:  # type: ignore[no-untyped-def]
     return a.elapsed_time(b) / n
 
 
+# The Cosmos-7B DiT block's linears (hidden 4096, MLP 16384) over one chunk of
+# 16384 tokens: (tokens M, in_features K, out_features N).
+LINEAR_SHAPES = {
+    "qkv": (16384, 4096, 12288),
+    "ffn_up": (16384, 4096, 16384),
+    "ffn_down": (16384, 16384, 4096),
+}
+
+
+def linear_measurements(dev, stream, peaks: dict) -> dict:  # type: ignore[no-untyped-def]
+    """FP8 DiT linears (``rp_fp8_gemm_ex``): the GEMM alone and the whole
+    ``fp8_linear`` (per-token activation quantize + GEMM), per-token x
+    per-channel scales, against cuBLASLt's row-scaled FP8 GEMM
+    (``torch._scaled_mm``) and torch's bf16 matmul on the same operands.
+    Algorithmic FLOPs 2*M*N*K; the kernel is timed alone, so the peak is the
+    burst e4m3 rate (2 x the measured bf16 burst)."""
+    import torch
+
+    from repercep_runtime_b200 import linear
+
+    if "bf16_tflops" in peaks:
+        peak, src = 2.0 * float(peaks["bf16_tflops"]), "of measured: 2 x MEASURED_PEAKS bf16_tflops (burst)"
+    else:
+        peak, src = 2.0 * 1590.0, "of fallback: 2 x 1.59 PFLOP/s burst bf16"
+    rows: dict = {}
+    for name, (M, K, N) in LINEAR_SHAPES.items():
+        g = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        x8, xs = linear.quantize_rows(x)
+        w8, ws = linear.quantize_rows(w)
+        fl = 2.0 * M * N * K
+        row: dict = {"M": M, "K": K, "N": N}
+        ms = _event_ms(lambda: linear.gemm_ex(x8, w8, xs, ws), stream, 10)
+        row["gemm_ms"] = ms
+        row["gemm_tflops"] = fl / ms / 1e9
+        row["frac"] = row["gemm_tflops"] / peak
+        ms = _event_ms(lambda: linear.fp8_linear(x, w8, ws), stream, 10)
+        row["fp8_linear_tflops"] = fl / ms / 1e9
+        wt, sa, sb = w8.t(), xs[:, None].contiguous(), ws[None, :].contiguous()
+        try:
+            ms = _event_ms(lambda: torch._scaled_mm(x8, wt, scale_a=sa, scale_b=sb,
+                                                    out_dtype=torch.bfloat16), stream, 10)
+            row["cublaslt_fp8_rowwise_tflops"] = fl / ms / 1e9
+        except Exception as e:  # pragma: no cover - depends on the torch build
+            row["cublaslt_fp8_rowwise_tflops"] = f"unavailable: {type(e).__name__}"
+        ms = _event_ms(lambda: x @ w.t(), stream, 10)
+        row["torch_bf16_tflops"] = fl / ms / 1e9
+        rows[name] = row
+        del x, w, x8, w8, xs, ws, wt, sa, sb
+    torch.cuda.synchronize(dev)
+    return {"kernel": "fp8_gemm_kernel (2-SM pairs, 256x256 tiles)", "bound": "tensor", "unit": "TFLOP/s",
+            "peak": peak, "peak_source": src, "shapes": rows}
+
+
 def side_measurements(runner: Runner, dev, stream, peaks: dict) -> dict:  # type: ignore[no-untyped-def]
     """Outside the timed region, one GPU only: the quantize kernel's bandwidth
     and torch's bf16 SDPA on the same inputs (the GPU comparison rows)."""
@@ -490,6 +545,10 @@ def side_measurements(runner: Runner, dev, stream, peaks: dict) -> dict:  # type
                                     "path is the --impl reference arm"}
     out["gpu_comparison"] = rows
     torch.cuda.synchronize(dev)
+    try:
+        out["fp8_linear"] = linear_measurements(dev, stream, peaks)
+    except Exception as e:  # a failure here must not hide the headline line
+        out["fp8_linear"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
     return out
 
 

@@ -524,6 +524,17 @@ bool gemm_pair_setting() {
   return v;
 }
 
+// Row tiles per raster group (0: the kernel's default).  REPERCEP_B200_GEMM_GROUP
+// overrides (read once).
+int gemm_group_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_GEMM_GROUP");
+    const int x = e ? std::atoi(e) : 0;
+    return (x > 0 && x <= 1024) ? x : 0;
+  }();
+  return v;
+}
+
 int gemm_b_box_rows(bool b_kmajor) {
   if (!b_kmajor) return 128;  // N-major: 128 K rows x 128 N bytes per box
   return gemm_pair_setting() ? GCfg<true>::kBRows : GCfg<false>::kBRows;
@@ -537,6 +548,7 @@ cudaError_t launch_fp8_gemm_t(const CUtensorMap& a, const CUtensorMap& b, GemmPa
   p.tiles_n = (p.N + kTileN - 1) / kTileN;
   p.tiles = p.tiles_m * p.tiles_n;
   p.n_kb = (p.K + kBK - 1) / kBK;
+  if (p.group_m <= 0) p.group_m = gemm_group_setting();
   if (p.group_m <= 0) p.group_m = PAIR ? 8 : 16;
   if (p.group_m > p.tiles_m) p.group_m = p.tiles_m;
   const int slots = PAIR ? sm_count() / 2 : sm_count();

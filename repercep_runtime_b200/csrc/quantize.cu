@@ -27,6 +27,7 @@
 #include <cuda_fp8.h>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace rp {
 
@@ -98,6 +99,38 @@ __device__ __forceinline__ uint2 quant8(uint4 v, float qm) {
   return make_uint2(o[0], o[1]);
 }
 
+// quant8 for a finite scale, two elements per instruction: packed fp32
+// multiply, then the paired e4m3 conversion, whose saturation is the clamp
+// to +-448 (every |y| between 448 and 464 rounds to 448 as well).  With a
+// finite scale no product is NaN (x is at most amax, and qm is finite and
+// nonzero), so the bytes equal quant8's; a NaN or infinite amax (NaN
+// products) takes quant8.
+__device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
+  const __nv_fp8x2_storage_t r = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE,
+                                                          __NV_E4M3);
+  return static_cast<uint32_t>(r);
+}
+
+template <bool F16>
+__device__ __forceinline__ uint2 quant8_fast(uint4 v, float qm) {
+  using T = Fmt<F16>;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const uint64_t q2 = pack_f32x2(qm, qm);
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float y0, y1;
+    unpack_f32x2(fmul2(pack_f32x2(T::lo(w[i]), T::hi(w[i])), q2), y0, y1);
+    h[i] = e4m3x2(y0, y1);
+  }
+  return make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+}
+
+template <bool F16>
+__device__ __forceinline__ uint2 quant8_any(uint4 v, float qm, bool fast) {
+  return fast ? quant8_fast<F16>(v, qm) : quant8<F16>(v, qm);
+}
+
 // max of |x| bit patterns held in a 16-byte vector (bf16 and fp16 alike:
 // non-negative values of both order like their bits, NaN above +inf).
 __device__ __forceinline__ uint32_t absmax8(uint4 v) {
@@ -144,14 +177,17 @@ struct BlockTile {
   }
 
   __device__ __forceinline__ void store(const QuantJob& j, int bh, int S, int ld, int s0,
-                                        int rows, float qm) {
+                                        int rows, float sc) {
     uint8_t* out = j.out + ((int64_t)bh * S + s0) * ld;
+    const float qm = __frcp_rn(sc);
+    const bool fast = isfinite(sc);
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
       const int idx = threadIdx.x + k * kQuantThreads;
       const int r = idx / kVpr, c = idx % kVpr;
       if (r < rows)
-        __stcs(reinterpret_cast<uint2*>(out + (int64_t)r * ld + c * 8), quant8<F16>(v[k], qm));
+        __stcs(reinterpret_cast<uint2*>(out + (int64_t)r * ld + c * 8),
+               quant8_any<F16>(v[k], qm, fast));
     }
     // zero padding of rows wider than D
     const int pad = (ld - D) / 8;
@@ -174,7 +210,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_block_kernel(const QuantA
   const uint32_t m = block_max(t.load(j, b, h, s0, rows), red);
   const float sc = scale_from_amax_bits<F16>(m);
   if (threadIdx.x == 0) j.scales[(int64_t)bh * a.nblk + blk] = sc;
-  t.store(j, bh, a.S, a.out_ld, s0, rows, __frcp_rn(sc));
+  t.store(j, bh, a.S, a.out_ld, s0, rows, sc);
 }
 
 // Per-(b,h) pass 1: partial amax of one 128-row chunk.
@@ -215,15 +251,57 @@ __global__ void __launch_bounds__(kQuantThreads) quant_bh_kernel(const QuantArgs
   const int rows = min(kQuantRows, a.S - s0);
   BlockTile<D, F16> t;
   t.load(j, b, h, s0, rows);
-  t.store(j, bh, a.S, a.out_ld, s0, rows, __frcp_rn(sc));
+  t.store(j, bh, a.S, a.out_ld, s0, rows, sc);
 }
 
 // Row-wise scales for the linear operands: one scale group per row of an
 // (rows, cols) matrix (a token of the activations, an output channel of a
-// weight), with the steps above.  One warp per row; the second pass re-reads
-// the row from L1/L2.
-template <bool F16>
+// weight), with the steps above.  TPR threads share a row and hold it in
+// registers (VPT 16-byte vectors each, all loads in flight at once), so the
+// row is read from HBM once and quantized from registers.
+template <bool F16, int TPR, int VPT>
 __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantRowsArgs a) {
+  static_assert(TPR % 32 == 0 && kQuantThreads % TPR == 0, "whole warps per row");
+  constexpr int kWarpsPerRow = TPR / 32;
+  __shared__ uint32_t red[kQuantThreads / 32];
+  const int grp = threadIdx.x / TPR, t = threadIdx.x % TPR;
+  const int64_t row = (int64_t)blockIdx.x * (kQuantThreads / TPR) + grp;
+  const bool live = row < a.rows;
+  const int nv = a.cols / 8;
+  const uint4* x = reinterpret_cast<const uint4*>(a.x + (live ? row : 0) * a.ldx);
+  uint4 v[VPT];
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = t + i * TPR;
+    v[i] = (live && idx < nv) ? __ldcs(x + idx) : make_uint4(0, 0, 0, 0);
+    m = max(m, absmax8(v[i]));
+  }
+  m = __reduce_max_sync(0xffffffffu, m);
+  if constexpr (kWarpsPerRow > 1) {
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[warp] = m;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kWarpsPerRow; ++w) m = max(m, red[grp * kWarpsPerRow + w]);
+  }
+  if (!live) return;
+  const float sc = scale_from_amax_bits<F16>(m);
+  if (t == 0) a.scales[row] = sc;
+  const float qm = __frcp_rn(sc);
+  const bool fast = isfinite(sc);
+  uint2* o = reinterpret_cast<uint2*>(a.out + row * a.ldo);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = t + i * TPR;
+    if (idx < nv) __stcs(o + idx, quant8_any<F16>(v[i], qm, fast));
+  }
+}
+
+// Rows longer than the register-resident forms hold: one warp per row, the
+// second pass re-reads the row (from L2).
+template <bool F16>
+__global__ void __launch_bounds__(kQuantThreads) quant_long_rows_kernel(const QuantRowsArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (kQuantThreads / 32) + warp;
   if (row >= a.rows) return;
@@ -235,21 +313,37 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantRo
   const float sc = scale_from_amax_bits<F16>(m);
   if (lane == 0) a.scales[row] = sc;
   const float qm = __frcp_rn(sc);
+  const bool fast = isfinite(sc);
   uint2* o = reinterpret_cast<uint2*>(a.out + row * a.ldo);
-  for (int i = lane; i < nv; i += 32) __stcs(o + i, quant8<F16>(__ldg(x + i), qm));
+  for (int i = lane; i < nv; i += 32) __stcs(o + i, quant8_any<F16>(__ldg(x + i), qm, fast));
+}
+
+template <bool F16, int TPR, int VPT>
+cudaError_t launch_rows_t(const QuantRowsArgs& a, cudaStream_t st) {
+  constexpr int kRowsPerCta = kQuantThreads / TPR;
+  const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
+  if (grid > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  quant_rows_kernel<F16, TPR, VPT><<<static_cast<unsigned>(grid), kQuantThreads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <bool F16>
+cudaError_t launch_rows_f(const QuantRowsArgs& a, cudaStream_t st) {
+  const int nv = a.cols / 8;  // 16-byte vectors per row
+  if (nv <= 32 * 4) return launch_rows_t<F16, 32, 4>(a, st);      // cols <= 1024
+  if (nv <= 128 * 4) return launch_rows_t<F16, 128, 4>(a, st);    // cols <= 4096
+  if (nv <= 256 * 8) return launch_rows_t<F16, 256, 8>(a, st);    // cols <= 16384
+  if (nv <= 256 * 16) return launch_rows_t<F16, 256, 16>(a, st);  // cols <= 32768
+  const int64_t grid = (a.rows + kQuantThreads / 32 - 1) / (kQuantThreads / 32);
+  if (grid > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  quant_long_rows_kernel<F16><<<static_cast<unsigned>(grid), kQuantThreads, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_quant_rows(const QuantRowsArgs& a, cudaStream_t st) {
-  constexpr int kRowsPerCta = kQuantThreads / 32;
-  const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
-  if (grid > 0x7FFFFFFF) return cudaErrorInvalidValue;
-  if (a.in_f16)
-    quant_rows_kernel<true><<<static_cast<unsigned>(grid), kQuantThreads, 0, st>>>(a);
-  else
-    quant_rows_kernel<false><<<static_cast<unsigned>(grid), kQuantThreads, 0, st>>>(a);
-  return cudaGetLastError();
+  return a.in_f16 ? launch_rows_f<true>(a, st) : launch_rows_f<false>(a, st);
 }
 
 #define RP_DISPATCH_DF(KERNEL, F16)                                               \

@@ -177,7 +177,9 @@ def test_output_into_a_strided_view():
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("rows,cols", [(1, 8), (5, 96), (300, 4096), (17, 13824), (9, 12)])
+@pytest.mark.parametrize(
+    "rows,cols", [(1, 8), (5, 96), (300, 4096), (17, 13824), (9, 12), (6, 20000), (5, 40000), (7, 5120)]
+)
 def test_quantize_rows_bit_exact(rows, cols, dtype):
     lin = _lin()
     x = gen_bf16((rows, cols), "n1_outlier", seed=rows + cols, dtype=dtype)
