@@ -644,7 +644,7 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     ms_step = ms_total / args.steps
     value = runner.job_flops * args.steps / (ms_total / 1e3) / 1e12
 
-    side = side_measurements(runner, dev, stream, load_peaks()) if world == 1 else {}
+    side = side_measurements(runner, dev, stream, load_peaks()) if world == 1 and not args.no_side else {}
 
     e2e = None
     if not args.no_e2e:
@@ -738,6 +738,8 @@ def main() -> None:
     ap.add_argument("--p-mode", type=int, choices=(0, 1), default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side", action="store_true",
+                    help="skip the side measurements (quantize bandwidth, SDPA and FP8 linear rows)")
     ap.add_argument("--no-graph", action="store_true", help="decode: launch eagerly instead of replaying a CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
