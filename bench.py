@@ -380,14 +380,12 @@ class Runner:
         q, k, v = self.inputs
         qq, kq, vq = ops.quantize_fp8((q, k, v), scale_mode=self.scale_mode)
         if self.mode == "cp":
-            B, H, rows, D = q.shape
-            k_all, v_all, ks_all, vs_all = self.cp.gather_kv(
-                kq.data.view(torch.uint8).reshape(B * H, rows, D),
-                vq.data.view(torch.uint8).reshape(B * H, rows, D), kq.scales, vq.scales)
+            # K/V gathers in (b, h) chunks, each chunk's attention starting when
+            # its gather lands: the bracket holds the attention launches and the
+            # gathers they did not hide
             if ev:
                 ev[0].record(self.stream)
-            out = ops.attention_fp8_chunked(qq, k_all.view(ops.FP8), v_all.view(ops.FP8), ks_all, vs_all,
-                                            last_rows=self.cp.shard.last_rows, p_mode=self.args.p_mode)
+            out = self.cp.attend_quantized(qq, kq, vq)
         else:
             if ev:
                 ev[0].record(self.stream)

@@ -86,13 +86,36 @@ def seq_shard(seq_len: int, rank: int, world: int) -> SeqShard:
 AllGather = Callable[["object", "object"], None]  # (output, input) -> None
 
 
-def nccl_all_gather(group=None) -> AllGather:  # type: ignore[no-untyped-def]
-    """``torch.distributed.all_gather_into_tensor`` bound to ``group``."""
+# (b, h) chunks per device call: every chunk's K/V gather is issued up front
+# and its attention starts as soon as that gather lands, so all gathers but
+# the first run under attention.  Measured on Wan (B2 H40 S75600), max over
+# ranks: 8 GPUs 21.95 ms unchunked, 21.25 with 2 chunks, 21.26 with 4; 2 GPUs
+# 81.15 / 80.84 / 81.98 (8 chunks).
+CP_CHUNKS = 2
+
+
+def nccl_all_gather(group=None, high_priority: bool = True) -> AllGather:  # type: ignore[no-untyped-def]
+    """``torch.distributed.all_gather_into_tensor`` bound to ``group``.
+
+    With no group and an NCCL default group, the gathers run in a new NCCL
+    group over the same ranks whose streams have high priority, so the block
+    scheduler gives the gather kernels SMs ahead of the next attention CTAs
+    (call it on every rank, like any group creation).  The returned callable
+    takes ``async_op`` and then returns the collective's work handle."""
+    import datetime
+
     import torch.distributed as dist
 
-    def gather(out, inp):  # type: ignore[no-untyped-def]
-        dist.all_gather_into_tensor(out, inp, group=group)
+    if group is None and high_priority and dist.get_backend() == "nccl":
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
+        group = dist.new_group(backend="nccl", pg_options=opts,
+                               timeout=datetime.timedelta(minutes=2))
 
+    def gather(out, inp, async_op: bool = False):  # type: ignore[no-untyped-def]
+        return dist.all_gather_into_tensor(out, inp, group=group, async_op=async_op)
+
+    gather.supports_async = True  # type: ignore[attr-defined]
     return gather
 
 
@@ -125,6 +148,13 @@ class ContextParallelAttention:
         collectives themselves (K, V and the two scale sets as three gathers).
         Only a rank whose shard is short of chunk_rows (the last) pads its
         contribution; nothing is repacked after the gather."""
+        k_all, v_all, sc_all, _ = self._gather(k8, v8, ks, vs, async_op=False)
+        return k_all, v_all, sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous()
+
+    def _gather(self, k8, v8, ks, vs, async_op: bool):  # type: ignore[no-untyped-def]
+        """gather_kv's three collectives; returns (K, V, scales (world, 2, BH,
+        nblk), work handles).  With async_op the handles must be waited on
+        before the outputs are read (their inputs stay referenced meanwhile)."""
         import torch
 
         sh = self.shard
@@ -144,16 +174,22 @@ class ContextParallelAttention:
 
         k_all = torch.empty((world, bh, sh.chunk_rows, d), dtype=torch.uint8, device=dev)
         v_all = torch.empty_like(k_all)
-        # outputs as (world * BH, rows, D): the rank-major concatenation every
-        # all_gather_into_tensor backend accepts
-        self.all_gather(k_all.view(world * bh, sh.chunk_rows, d), padded(k8))
-        self.all_gather(v_all.view(world * bh, sh.chunk_rows, d), padded(v8))
         sc = torch.zeros((2, bh, nblk), dtype=torch.float32, device=dev)
         sc[0, :, : ks.shape[-1]].copy_(ks.reshape(bh, -1))
         sc[1, :, : vs.shape[-1]].copy_(vs.reshape(bh, -1))
         sc_all = torch.empty((world, 2, bh, nblk), dtype=torch.float32, device=dev)
-        self.all_gather(sc_all.view(world * 2, bh, nblk), sc)
-        return k_all, v_all, sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous()
+        # outputs as (world * BH, rows, D): the rank-major concatenation every
+        # all_gather_into_tensor backend accepts
+        jobs = ((k_all.view(world * bh, sh.chunk_rows, d), padded(k8)),
+                (v_all.view(world * bh, sh.chunk_rows, d), padded(v8)),
+                (sc_all.view(world * 2, bh, nblk), sc))
+        works = []
+        for o, i in jobs:
+            if async_op:
+                works.append(self.all_gather(o, i, async_op=True))
+            else:
+                self.all_gather(o, i)
+        return k_all, v_all, sc_all, works
 
     def _call_host(self, q, k, v):  # type: ignore[no-untyped-def]
         """Host (pinned) shards: (b, h) chunks stream through the device with
@@ -209,7 +245,7 @@ class ContextParallelAttention:
                     if i >= len(slots):
                         cs.wait_event(ev_out[s])
                     self._device_call(qd[:n].unsqueeze(0), kd[:n].unsqueeze(0), vd[:n].unsqueeze(0),
-                                      out=od[:n].unsqueeze(0))
+                                      out=od[:n].unsqueeze(0), chunks=1)
                     ev_comp[s].record(cs)
                 with torch.cuda.stream(d2h):
                     d2h.wait_event(ev_comp[s])
@@ -225,7 +261,7 @@ class ContextParallelAttention:
             return self._call_host(q, k, v)
         return self._device_call(q, k, v, out=out)
 
-    def _device_call(self, q, k, v, out=None):  # type: ignore[no-untyped-def]
+    def _device_call(self, q, k, v, out=None, chunks: int | None = None):  # type: ignore[no-untyped-def]
         import torch
 
         from repercep_runtime_b200 import ops
@@ -236,27 +272,54 @@ class ContextParallelAttention:
         qq, kq, vq = ops.quantize_fp8((q, k, v), scale_mode=ops.SCALE_PER_BLOCK128)
         if sh.world == 1:
             return ops.attention_fp8_quantized(qq, kq, vq, scale=self.scale, p_mode=self.p_mode, out=out)
-        B, H, rows, D = q.shape
-        k_all, v_all, ks_all, vs_all = self.gather_kv(
-            kq.data.view(torch.uint8).reshape(B * H, rows, D),
-            vq.data.view(torch.uint8).reshape(B * H, rows, D),
-            kq.scales,
-            vq.scales,
-        )
-        return ops.attention_fp8_chunked(
-            qq,
-            k_all.view(ops.FP8),
-            v_all.view(ops.FP8),
-            ks_all,
-            vs_all,
-            last_rows=sh.last_rows,
-            scale=self.scale,
-            p_mode=self.p_mode,
-            out=out,
-        )
+        return self.attend_quantized(qq, kq, vq, out=out, chunks=chunks)
+
+    def attend_quantized(self, qq, kq, vq, out=None, chunks: int | None = None):  # type: ignore[no-untyped-def]
+        """Gather K/V and attend, for quantized (per-128-block) shards.
+
+        The (b, h) range is cut into ``chunks`` (default CP_CHUNKS) when the
+        bound all_gather is asynchronous: every chunk's gathers are issued
+        first, and chunk i's attention waits only for chunk i's gathers."""
+        import torch
+
+        from repercep_runtime_b200 import ops
+
+        sh = self.shard
+        B, H, rows, D = qq.data.shape
+        bh = B * H
+        k8 = kq.data.view(torch.uint8).reshape(bh, rows, D)
+        v8 = vq.data.view(torch.uint8).reshape(bh, rows, D)
+        n = CP_CHUNKS if chunks is None else chunks
+        n = min(n, bh) if getattr(self.all_gather, "supports_async", False) else 1
+        if out is None:
+            out = torch.empty((B, H, rows, D), dtype=torch.bfloat16, device=qq.data.device)
+        if not out.is_contiguous():
+            n = 1  # chunk views of the output need (B, H, rows, D) contiguous
+        if n <= 1:
+            k_all, v_all, ks_all, vs_all = self.gather_kv(k8, v8, kq.scales, vq.scales)
+            return ops.attention_fp8_chunked(qq, k_all.view(ops.FP8), v_all.view(ops.FP8), ks_all,
+                                             vs_all, last_rows=sh.last_rows, scale=self.scale,
+                                             p_mode=self.p_mode, out=out)
+        bounds = [(i * bh // n, (i + 1) * bh // n) for i in range(n)]
+        ks = kq.scales.reshape(bh, -1)
+        vs = vq.scales.reshape(bh, -1)
+        pending = [self._gather(k8[a:b], v8[a:b], ks[a:b], vs[a:b], async_op=True) for a, b in bounds]
+        q4 = qq.data.reshape(1, bh, rows, qq.data.shape[-1])
+        qs = qq.scales.reshape(bh, -1)
+        o4 = out.view(1, bh, rows, D)
+        for (a, b), (k_all, v_all, sc_all, works) in zip(bounds, pending):
+            for w in works:
+                w.wait()
+            qc = ops.Quantized(q4[:, a:b], qs[a:b], ops.SCALE_PER_BLOCK128, d=qq.d)
+            ops.attention_fp8_chunked(qc, k_all.view(ops.FP8), v_all.view(ops.FP8),
+                                      sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous(),
+                                      last_rows=sh.last_rows, scale=self.scale, p_mode=self.p_mode,
+                                      out=o4[:, a:b])
+        return out
 
 
 __all__ = [
+    "CP_CHUNKS",
     "ContextParallelAttention",
     "SeqShard",
     "nccl_all_gather",
