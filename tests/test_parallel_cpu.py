@@ -104,3 +104,42 @@ def _cp_worker(rank: int, world: int, port: int, S: int) -> None:
 @pytest.mark.parametrize("S,world", [(300, 2), (512, 2)])
 def test_context_parallel_gather_with_gloo_ranks(S, world):
     mp.spawn(_cp_worker, args=(world, _free_port(), S), nprocs=world, join=True)
+
+
+def _async_chunk_worker(rank: int, world: int, port: int, S: int) -> None:
+    """The overlapped path's gathers: per (b, h) chunk, asynchronous, through
+    ``nccl_all_gather`` bound to a gloo group -- the same bytes as one
+    synchronous gather of everything."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from repercep_runtime_b200.parallel import nccl_all_gather
+
+        BH, D = 5, 64
+        gather = nccl_all_gather()  # gloo default group: no high-priority subgroup, async supported
+        assert getattr(gather, "supports_async", False)
+        cp = ContextParallelAttention(S, rank, world, all_gather=gather)
+        sh = cp.shard
+        g = torch.Generator().manual_seed(rank)
+        k8 = torch.randint(0, 256, (BH, sh.rows, D), generator=g, dtype=torch.uint8)
+        v8 = torch.randint(0, 256, (BH, sh.rows, D), generator=g, dtype=torch.uint8)
+        nblk = -(-sh.rows // 128)
+        ks = torch.rand((BH, nblk), generator=g)
+        vs = torch.rand((BH, nblk), generator=g)
+        k_all, v_all, ks_all, vs_all = cp.gather_kv(k8, v8, ks, vs)
+        for bounds in ([(0, 2), (2, 5)], [(0, 1), (1, 3), (3, 5)]):
+            pending = [cp._gather(k8[a:b], v8[a:b], ks[a:b], vs[a:b], async_op=True) for a, b in bounds]
+            for (a, b), (kc, vc, sc, works) in zip(bounds, pending):
+                assert len(works) == 3
+                for w in works:
+                    w.wait()
+                assert torch.equal(kc, k_all[:, a:b]) and torch.equal(vc, v_all[:, a:b])
+                assert torch.equal(sc[:, 0], ks_all[:, a:b]) and torch.equal(sc[:, 1], vs_all[:, a:b])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("S,world", [(300, 2), (700, 3)])
+def test_chunked_async_gathers_match_one_gather(S, world):
+    mp.spawn(_async_chunk_worker, args=(world, _free_port(), S), nprocs=world, join=True)
