@@ -534,6 +534,9 @@ int rp_fp8_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, int b
                 (long long)lda, (long long)ldb);
   if ((sa && sa_stride < 0) || (sb && sb_stride < 0))
     return fail(RP_ERR_INVALID, "scale strides must be non-negative");
+  // tile counts are 32-bit in the kernel (128-row tiles bound both forms)
+  if (((int64_t)M + 127) / 128 * (((int64_t)N + 255) / 256) > 0x7FFFFFFF)
+    return fail(RP_ERR_UNSUPPORTED, "M x N too large (more than 2^31 output tiles)");
   int* status = nullptr;
   int rc = device_ready(&status);
   if (rc != RP_OK) return rc;

@@ -121,6 +121,10 @@ def test_gemm_entry_points_check_shapes_and_pitches(lib):
     assert ex(32, 32, 0, a=None) == -1 and b"non-null" in lib.rp_last_error()
     assert ex(32, 32, 0, M=-1) == -1
     assert ex(32, 32, 0, M=0) == 0  # empty output: nothing to launch
+    big = 2**31 - 1
+    rc = lib.rp_fp8_gemm_ex(dummy, 16, dummy, 16, 1, None, 0, 1.0, None, 0, 1.0, None, dummy, big, 0,
+                            big, big, 16, None)
+    assert rc == -2 and b"too large" in lib.rp_last_error()
     # row quantizer
     assert lib.rp_quant_fp8_rows(dummy, 16, 0, 4, 12, dummy, 16, dummy, None) == -2  # cols % 8
     assert lib.rp_quant_fp8_rows(dummy, 16, 3, 4, 16, dummy, 16, dummy, None) == -2  # dtype
