@@ -273,17 +273,19 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
 }
 
 // ------------------------------------------------------------ TMA producer
-template <int NQ, int PMODE, int DB>
+template <int NQ, int PMODE, int DB, bool KS = false>
 __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                          const CUtensorMap* tm_kx, const CUtensorMap* tm_vx,
                          const AttnKernelParams& p, const Bars& bar, uint8_t* smem, int n_steps) {
   using C = Cfg<NQ, PMODE, 1, false, DB>;
   RP_TRACE_INIT();
   const int bh = blockIdx.y;
-  const int qt0 = blockIdx.x * NQ;
-  mbar_arrive_expect_tx(bar.q_full, NQ * C::kQBytes);
+  // KS: one query tile per CTA, read by both tiles' QK MMAs from Q slot 0.
+  const int qt0 = KS ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * NQ;
+  constexpr int kQTiles = KS ? 1 : NQ;
+  mbar_arrive_expect_tx(bar.q_full, kQTiles * C::kQBytes);
 #pragma unroll
-  for (int t = 0; t < NQ; ++t)
+  for (int t = 0; t < kQTiles; ++t)
 #pragma unroll
     for (int kb = 0; kb < DB; ++kb)
       tma_load_4d(smem + C::kOffQ + t * C::kQBytes + kb * kTileBytes, tm_q, bar.q_full, kb * kTile,
@@ -342,7 +344,7 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
 }
 
 // -------------------------------------------------------------- MMA issuer
-template <int NQ, int PMODE, int DB>
+template <int NQ, int PMODE, int DB, bool KS = false>
 __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& bar,
                                          uint32_t sbase, uint32_t tmem, int i, bool last) {
   using C = Cfg<NQ, PMODE, 1, false, DB>;
@@ -353,16 +355,19 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
     return false;
   RP_TRACE(71, i);
 #pragma unroll
-  for (int t = 0; t < NQ; ++t) {
+  for (int tt = 0; tt < (KS ? 1 : NQ); ++tt) {
+    // KS: step i belongs to tile i & 1, its li-th step.
+    const int t = KS ? (i & 1) : tt;
+    const int li = KS ? (i >> 1) : i;
     // Two P_full barriers per tile, alternating by step: a softmax warpgroup
     // that runs ahead can complete step i+1 before this wait for step i, and
     // a single barrier would then be two phases ahead of the parity wait.
-    if (!mbar_wait(bar.p_full + 2 * t + (i & 1), (i >> 1) & 1, bar.abort_flag, p.status,
+    if (!mbar_wait(bar.p_full + 2 * t + (li & 1), (li >> 1) & 1, bar.abort_flag, p.status,
                    kErrWaitP))
       return false;
     RP_TRACE(70 + 2 * t, i);
     tc_fence_after();
-    const int pb = (C::kPBuf == 2) ? (i & 1) : 0;
+    const int pb = (C::kPBuf == 2) ? (li & 1) : 0;
     const uint32_t paddr = sbase + C::kOffP + (t * C::kPBuf + pb) * C::kPStride;
     const uint64_t pd = make_sw128_desc(paddr, 16, 1024);
     // O_t: DB column blocks of 128 after the NQ S tiles; V block nb feeds block nb.
@@ -373,7 +378,7 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
       const uint32_t d_tmem = tmem + (NQ + t * DB + nb) * kTile;
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        mma_f8(d_tmem, pd + 2 * k, vd + 256 * k, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+        mma_f8(d_tmem, pd + 2 * k, vd + 256 * k, idesc_pv, (li > 0 || k > 0) ? 1u : 0u);
       if constexpr (PMODE == 1) {
         const uint64_t pl = make_sw128_desc(paddr + kTileBytes, 16, 1024);
 #pragma unroll
@@ -381,14 +386,18 @@ __device__ __forceinline__ bool issue_pv(const AttnKernelParams& p, const Bars& 
       }
     }
     mma_commit(bar.o_done + t);
-    if (last) mma_commit(bar.o_final + t);
+    if (last) {
+      // KS: the other tile's last PV came earlier; both finals follow this one.
+      mma_commit(bar.o_final + t);
+      if (KS) mma_commit(bar.o_final + (1 - t));
+    }
     RP_TRACE(60 + t, i);
   }
   mma_commit(bar.v_empty + vsl);
   return true;
 }
 
-template <int NQ, int PMODE, int DB>
+template <int NQ, int PMODE, int DB, bool KS = false>
 __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* smem,
                            uint32_t tmem, int n_steps) {
   using C = Cfg<NQ, PMODE, 1, false, DB>;
@@ -404,9 +413,11 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
     }
     RP_TRACE(75, j);
 #pragma unroll
-    for (int t = 0; t < NQ; ++t) {
-      if (j > 0 &&
-          !mbar_wait(bar.s_free + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitSFree)) {
+    for (int tt = 0; tt < (KS ? 1 : NQ); ++tt) {
+      const int t = KS ? (j & 1) : tt;
+      const int li = KS ? (j >> 1) : j;
+      if (li > 0 &&
+          !mbar_wait(bar.s_free + t, (li - 1) & 1, bar.abort_flag, p.status, kErrWaitSFree)) {
         ok = false;
         break;
       }
@@ -416,8 +427,8 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
       for (int kb = 0; kb < DB; ++kb) {
         const uint64_t kd =
             make_sw128_desc(sbase + C::kOffK + ks * C::kKVBytes + kb * kTileBytes, 16, 1024);
-        const uint64_t qd =
-            make_sw128_desc(sbase + C::kOffQ + t * C::kQBytes + kb * kTileBytes, 16, 1024);
+        const uint64_t qd = make_sw128_desc(
+            sbase + C::kOffQ + (KS ? 0 : t) * C::kQBytes + kb * kTileBytes, 16, 1024);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_f8(tmem + t * kTile, qd + 2 * k, kd + 2 * k, idesc_qk, (kb > 0 || k > 0) ? 1u : 0u);
@@ -427,9 +438,22 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
     }
     if (!ok) break;
     mma_commit(bar.k_empty + ks);
-    if (j > 0) ok = issue_pv<NQ, PMODE, DB>(p, bar, sbase, tmem, j - 1, false);
+    // KS: a warpgroup's next S (step j) is issued before its previous PV
+    // (step j - 2), so it computes while that warpgroup is still on step
+    // j - 2.  The tensor pipe runs in order, so S_full(j) still implies every
+    // earlier PV is done (the P buffer reuse rule below holds unchanged).
+    if constexpr (KS) {
+      if (j >= 2) ok = issue_pv<NQ, PMODE, DB, KS>(p, bar, sbase, tmem, j - 2, false);
+    } else {
+      if (j > 0) ok = issue_pv<NQ, PMODE, DB, KS>(p, bar, sbase, tmem, j - 1, false);
+    }
   }
-  if (ok && n_steps > 0) issue_pv<NQ, PMODE, DB>(p, bar, sbase, tmem, n_steps - 1, true);
+  if constexpr (KS) {
+    for (int i = n_steps >= 2 ? n_steps - 2 : 0; ok && i < n_steps; ++i)
+      ok = issue_pv<NQ, PMODE, DB, KS>(p, bar, sbase, tmem, i, i == n_steps - 1);
+  } else {
+    if (ok && n_steps > 0) issue_pv<NQ, PMODE, DB, KS>(p, bar, sbase, tmem, n_steps - 1, true);
+  }
   // Everything this thread issued must finish before TMEM is released.
   mma_commit(bar.fin);
   mbar_drain(bar.fin, 0);
@@ -440,7 +464,7 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
 // [half * kNC, half * kNC + kNC).  With NSPLIT = 2 the two halves swap their
 // partial row maxima through shared memory every step and their partial row
 // sums once at the end.
-template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB, bool KS = false>
 __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
                            uint8_t* smem, uint32_t tmem, int n_steps) {
   using C = Cfg<NQ, PMODE, NSPLIT, TAB, DB>;
@@ -454,7 +478,13 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   const int col0 = half * NC;
   const bool tracer = (wq == 0 && lane == 0 && half == 0);
   const int bh = blockIdx.y;
-  const int q_tile = blockIdx.x * NQ + t;
+  // KS (one query tile, its K/V steps split between the two tiles' warpgroups):
+  // warpgroup t takes steps t, t + 2, ... and warpgroup 1 hands its partial
+  // row max and sum to warpgroup 0, which merges the two O accumulators.
+  static_assert(!KS || (NQ == 2 && NSPLIT == 1 && TAB && DB == 1), "KS: two tiles, table, D 128");
+  const int q_tile = KS ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * NQ + t;
+  const int j0 = KS ? t : 0;
+  constexpr int kStepStride = KS ? 2 : 1;
   const int q_tile_c = min(q_tile, p.n_q_tiles - 1);
   const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
   const uint32_t tS = tmem + lane_base + t * kTile + col0;
@@ -498,7 +528,8 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     // extra (decode) tile belongs to the CTA's only query tile (NQ == 1).
     constexpr int kN = C::kSoftmaxWarps * 32;
     float* red = reinterpret_cast<float*>(smem + C::kOffT);
-    const int qt0c = min(static_cast<int>(blockIdx.x) * NQ, p.n_q_tiles - 1);
+    const int qt0c = min(KS ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * NQ,
+                         p.n_q_tiles - 1);
     uint32_t vb = 0;
     for (int j = threadIdx.x; j < n_steps; j += kN) {
       int c, tt, valid;
@@ -531,7 +562,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       tab[j] = make_float4(p.sm_scale_log2 * e.x, __log2f(kj), __fdividef(1.f, kj), 0.f);
     }
     named_bar_sync(1, kN);
-    if (n_steps > 0) cst_n = tab[0];
+    if (n_steps > j0) cst_n = tab[j0];
   } else {
     uint32_t vbits = 0;
     for (int j = lane; j < p.n_main_tiles; j += 32) {
@@ -563,20 +594,22 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   bool ok = true;
   if (tracer) RP_TRACE(202 + t, 0);  // softmax prologue (scale table) done
   StepCursor cur;  // K/V tile of step j
-  for (int j = 0; j < n_steps; ++j) {
+  if (KS && j0 == 1 && n_steps > 0 && !(p.has_extra && p.n_main_tiles == 0)) cur.next(p);
+  for (int j = j0; j < n_steps; j += kStepStride) {
+    const int li = KS ? (j >> 1) : j;  // this warpgroup's step count
     const bool extra = p.has_extra && j == p.n_main_tiles;
     const int tt = cur.t;
     const int valid = extra ? kTile : cur.valid(p);
     if constexpr (TAB) {
       const float4 cst = cst_n;
-      if (j + 1 < n_steps) cst_n = tab[j + 1];
+      if (j + kStepStride < n_steps) cst_n = tab[j + kStepStride];
       cj = cst.x * sq;
       log2k = cst.y;
       invk = cst.z;
     }
     if (tracer) RP_TRACE(100 + t, j);
 
-    if (!warp_wait(bar.s_full + t, j & 1, bar.abort_flag, p.status, kErrWaitS)) {
+    if (!warp_wait(bar.s_full + t, li & 1, bar.abort_flag, p.status, kErrWaitS)) {
       ok = false;
       break;
     }
@@ -655,7 +688,8 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     // latency-bound phases.  Tile 0 is never two steps ahead here (its S for
     // step j+2 is issued only after tile 1's P of step j), so the barrier
     // pair indexed by step parity is never two phases ahead.
-    const bool stag_step = NQ == 2 && NSPLIT == 1 && (p.stagger == 2 || (p.stagger == 1 && j == 0));
+    const bool stag_step =
+        !KS && NQ == 2 && NSPLIT == 1 && (p.stagger == 2 || (p.stagger == 1 && j == 0));
     if (stag_step && t == 1 &&
         !warp_wait(bar.stag + 2 * wq + (j & 1), (j >> 1) & 1, bar.abort_flag, p.status, kErrWaitStag)) {
       ok = false;
@@ -710,13 +744,13 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       sum = u0 + u1;
     }
 
-    if (C::kPBuf == 1 && j > 0) {
-      if (!warp_wait(bar.o_done + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
+    if (C::kPBuf == 1 && li > 0) {
+      if (!warp_wait(bar.o_done + t, (li - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
         ok = false;
         break;
       }
     }
-    uint8_t* pb = pbase + ((C::kPBuf == 2) ? (j & 1) : 0) * C::kPStride;
+    uint8_t* pb = pbase + ((C::kPBuf == 2) ? (li & 1) : 0) * C::kPStride;
     const uint32_t prow = smem_u32(pb) + row * 128;
     constexpr int kChunks = NC / 16;  // 16-byte P chunks of this thread
 #pragma unroll
@@ -739,9 +773,9 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     // O is rescaled only when the running max moved; only then must PV(j-1)
     // have finished before O is touched.  (P buffer j&1 is already free:
     // S_full(j) was committed after PV(j-2) was issued.)
-    if (j > 0 && resc) {
+    if (li > 0 && resc) {
       if (C::kPBuf == 2 &&
-          !warp_wait(bar.o_done + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
+          !warp_wait(bar.o_done + t, (li - 1) & 1, bar.abort_flag, p.status, kErrWaitO)) {
         ok = false;
         break;
       }
@@ -767,7 +801,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(bar.p_full + 2 * t + (j & 1));
+    if (lane == 0) mbar_arrive(bar.p_full + 2 * t + (li & 1));
     if (tracer) RP_TRACE(40 + t, j);
     l_run = l_run * alpha + sum * invk;
     m_run = m_new;
@@ -775,6 +809,9 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     log2k = log2k_n;
     invk = invk_n;
     if (!extra) cur.next(p);
+    if constexpr (KS) {  // the other warpgroup's step
+      if (j + 1 < n_steps && !(p.has_extra && j + 1 == p.n_main_tiles)) cur.next(p);
+    }
   }
 
   // The last PV of this tile signals o_final (single use, so the wait is
@@ -789,6 +826,47 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     if (ok) l_run += xch[(2 * 2 + (1 - half)) * kTile + row];
   }
   if (!ok) return;
+
+  // KS: warpgroup 1 hands its row max (the reference point of its O and l)
+  // and row sum to warpgroup 0 through the unused Q slot 1; warpgroup 0
+  // weights the two accumulators by 2^(m_t - max) and stores the result.
+  float w0 = 1.f, w1 = 0.f;
+  bool has1 = false;
+  if constexpr (KS) {
+    float* ml = reinterpret_cast<float*>(smem + C::kOffQ + C::kQBytes);
+    const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+    if (t == 1) {
+      ml[row] = mu;
+      ml[kTile + row] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar.epi + 1);
+      return;
+    }
+    if (!warp_wait(bar.epi + 1, 0, bar.abort_flag, p.status, kErrWaitEpi)) return;
+    has1 = n_steps > 1;  // warpgroup 1 ran at least one step (else its O was never written)
+    if (has1) {
+      const float mu1 = ml[row], l1 = ml[kTile + row];
+      const float mm = fmaxf(mu, mu1);
+      w0 = ex2_approx(mu - mm);
+      w1 = ex2_approx(mu1 - mm);
+      l_run = l_run * w0 + l1 * w1;
+    }
+  }
+  // O columns [col, col + 32) of this thread's row, merged (KS) in place.
+  auto merge_o = [&](uint32_t (&o)[32], uint32_t col) {
+    if constexpr (KS) {
+      if (has1) {
+        uint32_t o1[32];
+        tmem_ld32(tO + DB * kTile + col, o1);  // tile 1's accumulator
+        tmem_wait_ld();
+        reg_fence(o1);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          o[i] = __float_as_uint(
+              __fmaf_rn(__uint_as_float(o[i]), w0, __fmul_rn(__uint_as_float(o1[i]), w1)));
+      }
+    }
+  };
   if (tracer) RP_TRACE(204 + t, 0);  // last PV done: epilogue starts
 
   // Epilogue: O * (sv_max / 448) / l -> bf16 or fp16, staged in this tile's
@@ -813,6 +891,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         tmem_ld32(tO + 32 * cc, o);
         tmem_wait_ld();
         reg_fence(o);
+        merge_o(o, 32 * cc);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float* v = reinterpret_cast<const float*>(o) + 8 * q;
@@ -832,6 +911,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
         tmem_ld32(tO + 64 * hh + 32 * cc, o);
         tmem_wait_ld();
         reg_fence(o);
+        merge_o(o, 64 * hh + 32 * cc);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int k = cc * 4 + q;
@@ -862,7 +942,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB, bool KS = false>
 __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
@@ -921,17 +1001,18 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
 
   int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
   if (p.causal) {
-    const int last_row = min(p.Sq, (blockIdx.x * NQ + NQ) * kTile) - 1;
+    const int q_end = KS ? static_cast<int>(blockIdx.x) + 1 : static_cast<int>(blockIdx.x) * NQ + NQ;
+    const int last_row = min(p.Sq, q_end * kTile) - 1;
     n_steps = min(n_steps, last_row / kTile + 1);
   }
 
   if (warp == C::kTmaWarp) {
     if (lane == 0)
-      producer<NQ, PMODE, DB>(&tm_q, &tm_k, &tm_v, &tm_kx, &tm_vx, p, bar, smem, n_steps);
+      producer<NQ, PMODE, DB, KS>(&tm_q, &tm_k, &tm_v, &tm_kx, &tm_vx, p, bar, smem, n_steps);
   } else if (warp == C::kMmaWarp) {
-    if (lane == 0) mma_issuer<NQ, PMODE, DB>(p, bar, smem, tmem, n_steps);
+    if (lane == 0) mma_issuer<NQ, PMODE, DB, KS>(p, bar, smem, tmem, n_steps);
   } else {
-    softmax_wg<NQ, PMODE, EPOLY, NSPLIT, TAB, DB>(&tm_o, p, bar, smem, tmem, n_steps);
+    softmax_wg<NQ, PMODE, EPOLY, NSPLIT, TAB, DB, KS>(&tm_o, p, bar, smem, tmem, n_steps);
   }
 
   tc_fence_before();
@@ -942,11 +1023,11 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   }
 }
 
-template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB>
+template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB, bool KS = false>
 cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
                        cudaStream_t st) {
   using C = Cfg<NQ, PMODE, NSPLIT, TAB, DB>;
-  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, NSPLIT, TAB, DB>;
+  auto kern = fa8_fwd_kernel<NQ, PMODE, EPOLY, NSPLIT, TAB, DB, KS>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -958,7 +1039,7 @@ cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int 
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_release);
   }
-  const dim3 grid((p.n_q_tiles + NQ - 1) / NQ, B * H);
+  const dim3 grid(KS ? p.n_q_tiles : (p.n_q_tiles + NQ - 1) / NQ, B * H);
   kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(m.q, m.k, m.v, m.kx, m.vx, m.o, p);
   return cudaGetLastError();
 }
@@ -992,6 +1073,18 @@ int exp_poly_setting() {
     if (!e) return kDefaultExpPoly;
     const int x = std::atoi(e);
     return (x == 0 || x == 2 || x == 4) ? x : kDefaultExpPoly;
+  }();
+  return v;
+}
+
+// Shared-prefix decode (one query tile per CTA): its K/V steps split between
+// the two softmax warpgroups of the two-tile layout (1, default) or one
+// warpgroup taking every step (0).  REPERCEP_B200_DECODE_KSPLIT overrides
+// (read once).
+int decode_ksplit_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_DECODE_KSPLIT");
+    return (e && std::atoi(e) == 0) ? 0 : 1;
   }();
   return v;
 }
@@ -1070,7 +1163,13 @@ cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& param
     return launch_variant<2, 0, 2, 1>(maps, p, B, H, st);
   }
   if (nq == 2 && p_mode == 1) return launch_variant<2, 1, 0, 1>(maps, p, B, H, st);
-  if (nq == 1 && p_mode == 0) return launch_variant<1, 0, 2, 1>(maps, p, B, H, st);
+  if (nq == 1 && p_mode == 0) {
+    const int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
+    if (decode_ksplit_setting() && step_table_setting() && !p.causal &&
+        n_steps <= Cfg<2, 0, 1, true, 1>::kTableSteps)
+      return launch_one<2, 0, 2, 1, true, 1, true>(maps, p, B, H, st);
+    return launch_variant<1, 0, 2, 1>(maps, p, B, H, st);
+  }
   if (nq == 1 && p_mode == 1) return launch_variant<1, 1, 0, 1>(maps, p, B, H, st);
   return cudaErrorInvalidValue;
 }

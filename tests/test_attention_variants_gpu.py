@@ -9,7 +9,9 @@ library reads these switches once per process):
   as the reference kernel does;
 * REPERCEP_B200_ROW_SPLIT=2 -- two threads per query row (row max and sum
   exchanged through shared memory);
-* REPERCEP_B200_EXP_POLY=0 / 4 -- every exp on MUFU / half on the FMA pipe.
+* REPERCEP_B200_EXP_POLY=0 / 4 -- every exp on MUFU / half on the FMA pipe;
+* REPERCEP_B200_DECODE_KSPLIT=0 -- the shared-prefix decode on one softmax
+  warpgroup taking every K/V step (instead of two taking alternate steps).
 """
 
 from __future__ import annotations
@@ -35,6 +37,7 @@ SUITE = ["tests/test_attention_gpu.py", "tests/test_decode_gpu.py", "tests/test_
         "REPERCEP_B200_ROW_SPLIT=2",
         "REPERCEP_B200_EXP_POLY=0",
         "REPERCEP_B200_EXP_POLY=4",
+        "REPERCEP_B200_DECODE_KSPLIT=0",
     ],
 )
 def test_attention_suite_under_schedule_switch(switch):
