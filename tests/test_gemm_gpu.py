@@ -196,22 +196,25 @@ def test_quantize_rows_bit_exact(rows, cols, dtype):
     assert scales_equal(s.cpu().numpy(), os_).all()
 
 
-def test_fp8_linear_against_the_oracle_and_torch():
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fp8_linear_against_the_oracle_and_torch(dtype):
     from repercep_runtime_b200.linear import Fp8Linear
 
     torch.manual_seed(0)
-    lin = torch.nn.Linear(320, 200, bias=True).to(device="cuda", dtype=torch.bfloat16)
-    x = gen_bf16((2, 37, 320), "n1", seed=11).cuda()
+    lin = torch.nn.Linear(320, 200, bias=True).to(device="cuda", dtype=dtype)
+    x = gen_bf16((2, 37, 320), "n1", seed=11, dtype=dtype).cuda()
     f8 = Fp8Linear.from_linear(lin)
     y = f8(x)
-    assert y.shape == (2, 37, 200) and y.dtype == torch.bfloat16
-    o = og.linear(bits(x.reshape(-1, 320)), bits(lin.weight), bits(lin.bias))
-    got = y.reshape(-1, 200)
-    diff = np.abs(bf16_bits_to_f32(bits(got)) - bf16_bits_to_f32(o))
+    assert y.shape == (2, 37, 200) and y.dtype == dtype
+    fmt = "bf16" if dtype == torch.bfloat16 else "f16"
+    o = og.linear(bits(x.reshape(-1, 320)), bits(lin.weight), bits(lin.bias), fmt)
+    got = y.reshape(-1, 200).float().cpu().numpy()
+    ref = (bf16_bits_to_f32(o) if fmt == "bf16" else o.view(np.float16).astype(np.float32))
+    diff = np.abs(got - ref)
     assert np.mean(diff == 0) > 0.99
-    assert (diff <= 2.0**-7 * np.abs(bf16_bits_to_f32(o)) + 1e-6).all()
-    ref = lin(x).float()
-    cos = torch.nn.functional.cosine_similarity(y.float().flatten(), ref.flatten(), dim=0)
+    assert (diff <= 2.0**-7 * np.abs(ref) + 1e-6).all()
+    full = lin(x).float()
+    cos = torch.nn.functional.cosine_similarity(y.float().flatten(), full.flatten(), dim=0)
     assert cos.item() > 0.998
 
 

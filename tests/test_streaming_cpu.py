@@ -19,8 +19,8 @@ def test_plan_covers_every_slice_once(bh, seq):
 
 
 def test_plan_fills_the_gpu_and_bounds_the_chunk_count():
-    # Cosmos: 225 CTAs per slice -> one slice already fills the GPU; ~32 chunks
-    assert plan_chunks(64, 57600) == ChunkPlan(64, 2)
+    # Cosmos: 225 CTAs per slice -> one slice already fills the GPU; ~64 chunks
+    assert plan_chunks(64, 57600) == ChunkPlan(64, 1)
     # cfg2: 32 CTAs per slice -> at least 5 slices per chunk
     p = plan_chunks(64, 8192)
     assert p.chunk * 32 >= MIN_CTAS and p.n == 13
