@@ -283,18 +283,29 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
   // KS: one query tile per CTA, read by both tiles' QK MMAs from Q slot 0.
   const int qt0 = KS ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * NQ;
   constexpr int kQTiles = KS ? 1 : NQ;
-  mbar_arrive_expect_tx(bar.q_full, kQTiles * C::kQBytes);
+  auto load_q = [&]() {
+    mbar_arrive_expect_tx(bar.q_full, kQTiles * C::kQBytes);
 #pragma unroll
-  for (int t = 0; t < kQTiles; ++t)
+    for (int t = 0; t < kQTiles; ++t)
 #pragma unroll
-    for (int kb = 0; kb < DB; ++kb)
-      tma_load_4d(smem + C::kOffQ + t * C::kQBytes + kb * kTileBytes, tm_q, bar.q_full, kb * kTile,
-                  (qt0 + t) * kTile, bh, 0);
+      for (int kb = 0; kb < DB; ++kb)
+        tma_load_4d(smem + C::kOffQ + t * C::kQBytes + kb * kTileBytes, tm_q, bar.q_full,
+                    kb * kTile, (qt0 + t) * kTile, bh, 0);
+  };
+  // KS (the decode, launched as a dependent of its quantize launch): the
+  // shared-prefix K/V tiles do not depend on that launch, so the first ring's
+  // worth goes out before waiting for it; Q and the suffix tile come after.
+  const int n_early = KS ? min(C::kSt, p.n_main_tiles) : 0;
+  if (!KS) load_q();
 
   int nk = 0, nv = 0;
   bool ok = true;
   StepCursor cur;
   for (int j = 0; j < n_steps && ok; ++j) {
+    if (KS && j == n_early) {
+      griddep_wait();
+      load_q();
+    }
     const bool extra = p.has_extra && j == p.n_main_tiles;
     const int c = cur.c, t = cur.t;
     if (!extra) cur.next(p);
@@ -332,6 +343,10 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
     }
     ++nv;
     RP_TRACE(81, j);
+  }
+  if (KS && ok && n_steps <= n_early) {  // (a decode always has its suffix step after)
+    griddep_wait();
+    load_q();
   }
   if (!ok) {
     // Abort: let every load already issued land before shared memory goes away.
@@ -494,6 +509,9 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   float* xch = reinterpret_cast<float*>(smem + C::kOffX) + t * 3 * 2 * kTile;
   uint64_t* xbar = bar.xch + (t * 4 + wq) * 3;
 
+  // KS (the decode): Q's scale and the suffix scales come from the launch
+  // this one may overlap; wait for it before the first read.
+  if constexpr (KS) griddep_wait();
   const float sq = p.qs[bh * p.qs_bh + q_tile_c * p.qs_blk];
 
   // Largest V scale this CTA meets (positive floats order like their bits),
@@ -1023,6 +1041,17 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   }
 }
 
+// The decode launched as a programmatic dependent of the launch before it
+// (1, default) or after it completes (0).  REPERCEP_B200_DECODE_PDL overrides
+// (read once).
+int decode_pdl_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_DECODE_PDL");
+    return (e && std::atoi(e) == 0) ? 0 : 1;
+  }();
+  return v;
+}
+
 template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB, bool KS = false>
 cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int H,
                        cudaStream_t st) {
@@ -1040,6 +1069,22 @@ cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int 
     configured.fetch_or(bit, std::memory_order_release);
   }
   const dim3 grid(KS ? p.n_q_tiles : (p.n_q_tiles + NQ - 1) / NQ, B * H);
+  if (KS && decode_pdl_setting()) {
+    // The decode may start while its quantize launch finishes (programmatic
+    // dependent launch); its kernel waits for that launch before reading Q
+    // and the suffix.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(C::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, m.q, m.k, m.v, m.kx, m.vx, m.o, p);
+  }
   kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(m.q, m.k, m.v, m.kx, m.vx, m.o, p);
   return cudaGetLastError();
 }

@@ -198,6 +198,19 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel of its stream still runs; griddep_wait() blocks the
+// calling thread until that kernel has completed and its writes are visible
+// (it returns at once when there is no such kernel).  griddep_launch() lets
+// the next kernel start early.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------- CTA pairs (clusters of 2)
 // The 2-SM GEMM runs one tile per pair of CTAs: the MMAs issued by rank 0
 // (cta_group::2) read both CTAs' shared memory and write both CTAs' TMEM.

@@ -200,6 +200,9 @@ struct BlockTile {
 
 template <int D, bool F16>
 __global__ void __launch_bounds__(kQuantThreads) quant_block_kernel(const QuantArgs a) {
+  // A dependent kernel (the shared-prefix decode) may start its prologue now;
+  // it waits for this grid's completion before reading what it writes.
+  griddep_launch();
   __shared__ uint32_t red[kQuantThreads / 32];
   const QuantJob& j = a.job[blockIdx.z];
   const int blk = blockIdx.x, bh = blockIdx.y;

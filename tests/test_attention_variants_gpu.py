@@ -11,7 +11,9 @@ library reads these switches once per process):
   exchanged through shared memory);
 * REPERCEP_B200_EXP_POLY=0 / 4 -- every exp on MUFU / half on the FMA pipe;
 * REPERCEP_B200_DECODE_KSPLIT=0 -- the shared-prefix decode on one softmax
-  warpgroup taking every K/V step (instead of two taking alternate steps).
+  warpgroup taking every K/V step (instead of two taking alternate steps);
+* REPERCEP_B200_DECODE_PDL=0 -- the decode launched after its quantize launch
+  completes instead of as its programmatic dependent.
 """
 
 from __future__ import annotations
@@ -38,6 +40,7 @@ SUITE = ["tests/test_attention_gpu.py", "tests/test_decode_gpu.py", "tests/test_
         "REPERCEP_B200_EXP_POLY=0",
         "REPERCEP_B200_EXP_POLY=4",
         "REPERCEP_B200_DECODE_KSPLIT=0",
+        "REPERCEP_B200_DECODE_PDL=0",
     ],
 )
 def test_attention_suite_under_schedule_switch(switch):
