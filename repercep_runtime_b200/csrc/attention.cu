@@ -292,20 +292,17 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
         tma_load_4d(smem + C::kOffQ + t * C::kQBytes + kb * kTileBytes, tm_q, bar.q_full,
                     kb * kTile, (qt0 + t) * kTile, bh, 0);
   };
-  // KS (the decode, launched as a dependent of its quantize launch): the
-  // shared-prefix K/V tiles do not depend on that launch, so the first ring's
-  // worth goes out before waiting for it; Q and the suffix tile come after.
-  const int n_early = KS ? min(C::kSt, p.n_main_tiles) : 0;
-  if (!KS) load_q();
+  // KS (the decode, launched as a programmatic dependent of the launch
+  // before it): no global read before that launch has completed -- it may
+  // have written any operand, the prefix included.  What overlaps it is this
+  // CTA's launch, barrier and TMEM setup.
+  if (KS) griddep_wait();
+  load_q();
 
   int nk = 0, nv = 0;
   bool ok = true;
   StepCursor cur;
   for (int j = 0; j < n_steps && ok; ++j) {
-    if (KS && j == n_early) {
-      griddep_wait();
-      load_q();
-    }
     const bool extra = p.has_extra && j == p.n_main_tiles;
     const int c = cur.c, t = cur.t;
     if (!extra) cur.next(p);
@@ -343,10 +340,6 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
     }
     ++nv;
     RP_TRACE(81, j);
-  }
-  if (KS && ok && n_steps <= n_early) {  // (a decode always has its suffix step after)
-    griddep_wait();
-    load_q();
   }
   if (!ok) {
     // Abort: let every load already issued land before shared memory goes away.
