@@ -66,3 +66,28 @@ def test_prefix_decode_matches_oracle(C, T, P, H):
 def test_prefix_decode_full_vla_shape_hilo():
     m = _run(64, 8, 512, 32, p_mode=1)
     assert m["max_abs"] <= 2e-2 and m["cos"] >= 0.9999, m
+
+
+def test_decode_right_after_the_prefix_is_written():
+    """The decode is launched as a programmatic dependent of the launch before
+    it; with the prefix quantized by that very launch (the suffix and Q
+    quantized earlier) it must still read the finished prefix: the result is
+    bit-equal to the same decode with a synchronisation in between."""
+    from repercep_runtime_b200 import ops
+    from repercep_runtime_b200.attention import SharedPrefixFP8Decode
+
+    C, T, P, H, D = 64, 8, 512, 32, 128
+    q, kx, vx = (gen_bf16((C * T, H, D), "n1", s).cuda() for s in (11, 12, 13))
+    kp, vp = (gen_bf16((P, H, D), "n1", s).cuda() for s in (14, 15))
+    op = SharedPrefixFP8Decode()
+    qq, kxq, vxq = ops.quantize_fp8(
+        (q.unsqueeze(0), kx.unsqueeze(0), vx.unsqueeze(0)), scale_mode=ops.SCALE_PER_BLOCK128, layout="bshd"
+    )
+    outs = []
+    for sync in (True, False):
+        prefix = op.quantize_prefix(kp, vp)  # the launch right before the decode
+        if sync:
+            torch.cuda.synchronize()
+        outs.append(ops.prefix_decode_fp8_quantized(qq, prefix.k, prefix.v, kxq, vxq, candidates=C, tokens=T))
+        torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
