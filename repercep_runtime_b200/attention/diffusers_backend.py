@@ -1,23 +1,33 @@
-"""diffusers attention-dispatch bridge for B200 — mirrors the reference's
-``"repercep_fp8"`` backend (src/repercep/attention/diffusers_backend.py).
+"""diffusers attention-dispatch bridge for B200 -- the reference's
+``"repercep_fp8"`` backend (src/repercep/attention/diffusers_backend.py) with
+the B200 kernels behind it.
 
 The backend function keeps the reference's signature (:160-171) and routing
-rules (:44, :52-79, :199-231): bf16 or fp16, q/k/v of one shape, a head dim
+rules (:44, :52-79, :186-231): bf16 or fp16, q/k/v of one shape, a head dim
 in {32, 64, 128, 256}, seq_len >= the crossover, no mask / dropout / GQA /
-context-parallel config; everything else goes to a native SDPA fallback.  What changes is the
-layout handling: diffusers passes (B, S, H, D) and the B200 kernels read and
-write that layout through strides, so the reference's three
-``permute(0, 2, 1, 3).contiguous()`` copies in and one out (:264-267, :286)
-are gone.  The reference's non-finite guard (``isfinite().all()`` per call,
-:271-285, falling back to SDPA for that call) is kept by default because it is
-part of the seam's contract, and it costs a host synchronisation per call.
-``REPERCEP_B200_FINITE_GUARD=deferred`` keeps the check on the device instead:
-every call adds "any non-finite output" to a per-device counter without
-synchronising, and ``nonfinite_calls()`` reads it (once per denoise step, say);
-``REPERCEP_B200_FINITE_GUARD=0`` drops the check.
+context-parallel config, ``REPERCEP_FP8_ATTENTION`` not ``fa``/``flash``.
+What changes is the layout handling: diffusers passes (B, S, H, D) and the
+B200 kernels read and write that layout through strides, so the reference's
+three ``permute(0, 2, 1, 3).contiguous()`` copies in and one out (:264-267,
+:286) are gone.  The reference's non-finite guard (``isfinite().all()`` per
+call, :271-285, falling back to SDPA for that call) is kept by default because
+it is part of the seam's contract, and it costs a host synchronisation per
+call.  ``REPERCEP_B200_FINITE_GUARD=deferred`` keeps the check on the device
+instead: every call adds "any non-finite output" to a per-device counter
+without synchronising, and ``nonfinite_calls()`` reads it (once per denoise
+step, say); ``REPERCEP_B200_FINITE_GUARD=0`` drops the check.
 
-Registration touches diffusers' private registry exactly like the reference
-(:289-339) and is a no-op when diffusers is not installed.
+Registration: the ``"repercep_fp8"`` entry of diffusers' registry is set to
+this module's function even when the reference's module registered first
+(importing ``repercep.attention`` does, :394-399); the function it replaces is
+kept, and every call this bridge does not serve on the B200 kernel (no sm_100
+device, a shape or option the kernel does not take, ``fa``/``flash`` mode) is
+handed to it, so the reference's own routing (its flash-attn wrapper, its SDPA
+fallback) stays in force for those.  Without a previous function, those calls
+go to SDPA as in diffusers' native path.  The reference's Wan installer
+(attention/wan_processor.py:45-50) and ``CosmosEngine.load`` (models/cosmos.py:168-170)
+look the entry up by name, so they reach this function.  Registration is a
+no-op when diffusers is not installed.
 """
 
 from __future__ import annotations
@@ -138,14 +148,23 @@ def _repercep_fp8_attention(
         scale=scale,
         enable_gqa=enable_gqa,
     )
+
+    def hand_off() -> Any:
+        prev = handoff_target()
+        if prev is not None:
+            return prev(query, key, value, **fallback, return_lse=return_lse,
+                        _parallel_config=_parallel_config)
+        return _native_fallback(query, key, value, **fallback)
+
     if (
-        _parallel_config is not None
+        os.environ.get("REPERCEP_FP8_ATTENTION", "").lower() in ("fa", "flash")
+        or _parallel_config is not None
         or attn_mask is not None
         or dropout_p != 0.0
         or enable_gqa
         or not _route_should_use_fp8(query, key, value)
     ):
-        return _native_fallback(query, key, value, **fallback)
+        return hand_off()
 
     op = getattr(_repercep_fp8_attention, "_op", None)
     if op is None:
@@ -153,8 +172,8 @@ def _repercep_fp8_attention(
 
         op = B200FP8Attention()
         _repercep_fp8_attention._op = op  # type: ignore[attr-defined]
-    if not op.available:
-        return _native_fallback(query, key, value, **fallback)
+    if not op.available or query.device.type != "cuda":
+        return hand_off()
 
     from repercep_runtime_b200 import ops
 
@@ -198,14 +217,38 @@ def _ensure_backend_name_registered() -> Any:
     return member
 
 
+# The function this module's registration replaced (the reference's, when it
+# registered first); calls the B200 kernel does not serve go to it.
+_PREVIOUS: dict[str, Any] = {}
+
+
+def handoff_target() -> Any:
+    """Where calls the B200 kernel does not serve go: the function this
+    module's registration replaced, else (this module registered first) the
+    reference's own backend function when the reference is importable, else
+    None (diffusers' native SDPA path, ``_native_fallback``)."""
+    fn = _PREVIOUS.get("fn")
+    if fn is None:
+        try:
+            from repercep.attention.diffusers_backend import _repercep_fp8_attention as fn
+        except ImportError:
+            return None
+        _PREVIOUS["fn"] = fn
+    return fn
+
+
 def register_repercep_fp8_backend() -> Any:
-    """Register the backend function with diffusers (idempotent)."""
+    """Make this module's function diffusers' "repercep_fp8" backend
+    (idempotent), keeping any function it replaces as the hand-off target."""
     import inspect
 
     from diffusers.models.attention_dispatch import _AttentionBackendRegistry
 
     member = _ensure_backend_name_registered()
-    if member not in _AttentionBackendRegistry._backends:
+    prev = _AttentionBackendRegistry._backends.get(member)
+    if prev is not _repercep_fp8_attention:
+        if prev is not None:
+            _PREVIOUS["fn"] = prev
         _AttentionBackendRegistry._backends[member] = _repercep_fp8_attention
         _AttentionBackendRegistry._constraints[member] = []
         _AttentionBackendRegistry._supported_arg_names[member] = set(
@@ -225,9 +268,14 @@ def activate_repercep_fp8_backend() -> bool:
     return True
 
 
+# The reference's accepted values (:377) plus "b200".
+_ACTIVATE_VALUES = ("1", "true", "on", "triton", "scaled_mm", "fa", "flash", "b200")
+
+
 def maybe_activate_from_env() -> bool:
-    """Activate iff REPERCEP_FP8_ATTENTION is truthy (reference :364-388)."""
-    if os.environ.get("REPERCEP_FP8_ATTENTION", "").lower() not in ("1", "true", "on", "triton", "b200"):
+    """Activate iff REPERCEP_FP8_ATTENTION is set to one of the reference's
+    values (reference :364-388) or ``b200``."""
+    if os.environ.get("REPERCEP_FP8_ATTENTION", "").lower() not in _ACTIVATE_VALUES:
         return False
     try:
         return activate_repercep_fp8_backend()

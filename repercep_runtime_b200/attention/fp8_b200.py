@@ -93,6 +93,8 @@ class B200FP8Attention:
         return self._import_error
 
     def supports(self, shape: AttentionShape, dtype: DType) -> bool:
+        # Compared by value: ``shape`` and ``dtype`` may be the reference's own
+        # classes or this package's stand-ins (StrEnum members equal their strings).
         return (
             self.available
             and dtype in (DType.BF16, DType.FP16)
@@ -103,7 +105,7 @@ class B200FP8Attention:
             and shape.batch * shape.heads <= 65535
             # the causal mask is top-left aligned like the reference's, which
             # only means "causal" for self-attention
-            and (shape.kind is AttentionKind.FULL or shape.is_self_attention)
+            and (shape.kind == AttentionKind.FULL or shape.is_self_attention)
         )
 
     def __call__(

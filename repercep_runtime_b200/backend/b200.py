@@ -5,8 +5,10 @@ Closes the gaps the reference's ``CUDABackend`` has on Blackwell
 ``DeviceArch(NVIDIA, "100", "unknown")`` (:108-110), FP8 is advertised
 (the reference only does so for sm90/sm89, :164-169), and ``attention_op``
 routes through a registry whose NVIDIA branch knows the B200 op.
-Registered ahead of the reference's CUDA backend, it
-claims only hosts with a compute-capability 10.0 device.
+Placed ahead of the reference's CUDA backend in its backend list
+(``repercep_runtime_b200.integration.install`` does so at run time), it
+claims only hosts with a compute-capability 10.0 device.  Its value types are
+the reference's own classes whenever the reference package is importable.
 """
 
 from __future__ import annotations
@@ -21,6 +23,7 @@ from repercep_runtime_b200.hardware import (
     DeviceSpec,
     DType,
     Vendor,
+    is_b200_arch,
 )
 
 if TYPE_CHECKING:
@@ -47,7 +50,7 @@ class B200Backend:
             return False
         if torch.version.cuda is None or torch.version.hip or not torch.cuda.is_available():
             return False
-        return any(d.arch is B200 for d in self.devices())
+        return any(is_b200_arch(d.arch) for d in self.devices())
 
     def devices(self) -> tuple[DeviceSpec, ...]:
         import torch
@@ -75,7 +78,7 @@ class B200Backend:
         if B200FP8Attention().available:
             ops.append(B200FP8Attention.name)
         ops.append("naive-sdpa")
-        has_b200 = any(d.arch is B200 for d in self.devices())
+        has_b200 = any(is_b200_arch(d.arch) for d in self.devices())
         dtypes = {DType.FP32, DType.FP16, DType.BF16, DType.INT8}
         if has_b200:
             dtypes |= {DType.FP8_E4M3, DType.FP8_E5M2}

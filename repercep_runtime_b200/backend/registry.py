@@ -1,7 +1,8 @@
 """Backend discovery (reference: src/repercep/backend/registry.py:22-57).
 
-Same functions and error behaviour; the list holds the B200 backend, which
-the reference's own list takes in front of ``CUDABackend``.
+Same functions and error behaviour; the list holds the B200 backend.  In the
+reference's own list the B200 backend goes in front of ``CUDABackend``
+(``repercep_runtime_b200.integration.install`` puts it there at run time).
 """
 
 from __future__ import annotations

@@ -412,6 +412,10 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
   RP_TRACE_INIT();
   constexpr uint32_t idesc_qk = make_idesc_e4m3(128, 128, 0, 0);
   const uint32_t sbase = smem_u32(smem);
+  // KS (launched as a programmatic dependent): the bounded waits below start
+  // only once the launch before has completed, so a long predecessor cannot
+  // use up their time limit.
+  if constexpr (KS) griddep_wait();
   bool ok = mbar_wait(bar.q_full, 0, bar.abort_flag, p.status, kErrWaitQ);
   for (int j = 0; ok && j < n_steps; ++j) {
     const int ks = j % C::kSt;

@@ -51,11 +51,16 @@ int noalloc_scratch(uint32_t** out) {
   if (dev < 0 || dev >= 64) return set_last_error(RP_ERR_INVALID, "device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr) {
-    int major = 0;
+    // Compute capability exactly 10.0, like every other entry point: the
+    // library holds sm_100a code only, so a 10.x device with x != 0 is
+    // rejected here rather than failing at launch.
+    int major = 0, minor = 0;
     e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
     if (e != cudaSuccess)
       return set_last_error(RP_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
-    if (major != 10) return set_last_error(RP_ERR_ARCH, "device %d is not sm_100 (B200)", dev);
+    if (major != 10 || minor != 0)
+      return set_last_error(RP_ERR_ARCH, "device %d is not sm_100 (B200); this library is sm_100a only", dev);
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)

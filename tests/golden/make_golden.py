@@ -38,6 +38,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(HERE.parent))
 
 QUANT_CASES = [
@@ -104,9 +107,14 @@ def bits(t):  # type: ignore[no-untyped-def]
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None,
+                    help="reference source tree (default: $REPERCEP_REFERENCE_ROOT or ../reference)")
     args = ap.parse_args()
-    ref = Path(args.reference)
+    from oracle.build_ref import reference_root
+
+    ref = Path(args.reference) if args.reference else reference_root()
+    if ref is None:
+        raise SystemExit("reference source tree not found; pass --reference")
     os.environ["TRITON_INTERPRET"] = "1"
     os.environ["REPERCEP_FP8_DISABLE_AUTOTUNE"] = "1"
     sys.path.insert(0, str(ref / "kernels"))

@@ -6,8 +6,10 @@ whose memory pool forbids raw cudaMalloc).  For them the per-(b,h) quantizer
 keeps its partial-amax scratch in a fixed array inside the library.  These
 tests call it through the C ABI and require byte-for-byte the same e4m3 output
 and the same scales as the workspace-taking entry point, on two calls in a
-row (the second with different data, so leftovers in the shared array would
-show), and a clear rejection of shapes larger than the array.
+row, also when a large call is followed by a smaller one that uses a strict
+subset of the shared array's slots; that repeated calls leave the device's
+free memory unchanged (no allocation anywhere below the call); and a clear
+rejection of shapes larger than the array.
 
 This file sorts last so that a run stopping at its first failure has already
 run every other test.
@@ -59,9 +61,10 @@ def _with_workspace(lib, xs):
     return outs, scales
 
 
-def _without_allocation(lib, xs):
+def _without_allocation(lib, xs, outs=None, scales=None):
     B, H, S, D = xs[0].shape
-    outs, scales = _outputs(xs)
+    if outs is None:
+        outs, scales = _outputs(xs)
     stream = torch.cuda.current_stream().cuda_stream
     rc = lib.rp_quant_fp8_e4m3_noalloc(len(xs), _ptrs(xs), _strides(xs), B, H, S, D, _ptrs(outs),
                                        _ptrs(scales), stream)
@@ -88,6 +91,49 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row():
         for r, g in zip(ref_sc, got_sc):
             assert np.array_equal(r.cpu().numpy().view(np.uint32), g.cpu().numpy().view(np.uint32))
     assert _lib.device_status() == 0
+
+
+def _check_same(lib, xs, got_out, got_sc):
+    ref_out, ref_sc = _with_workspace(lib, xs)
+    torch.cuda.synchronize()
+    for r, g in zip(ref_out, got_out):
+        assert _same_bytes(r, g)
+    for r, g in zip(ref_sc, got_sc):
+        assert np.array_equal(r.cpu().numpy().view(np.uint32), g.cpu().numpy().view(np.uint32))
+
+
+def test_noalloc_large_call_then_smaller_subset_call():
+    """The second call's slots are a strict subset of the first's, so the
+    first call's partial maxima are still in the rest of the array; the
+    second call must read only what it wrote."""
+    from repercep_runtime_b200 import _lib
+
+    lib = _lib.load()
+    big = [gen_bf16((2, 16, 6000, 128), "n1_outlier", 301 + i).cuda() * 8 for i in range(3)]
+    small = [gen_bf16((1, 2, 700, 128), "n05", 401 + i).cuda() for i in range(2)]
+    out_b, sc_b = _without_allocation(lib, big)
+    out_s, sc_s = _without_allocation(lib, small)
+    torch.cuda.synchronize()
+    _check_same(lib, big, out_b, sc_b)
+    _check_same(lib, small, out_s, sc_s)
+    assert _lib.device_status() == 0
+
+
+def test_noalloc_calls_leave_device_memory_unchanged():
+    from repercep_runtime_b200 import _lib
+
+    lib = _lib.load()
+    xs = [gen_bf16((2, 8, 3000, 128), "n05", 501 + i).cuda() for i in range(3)]
+    outs, scales = _outputs(xs)
+    _without_allocation(lib, xs, outs, scales)  # warm-up: first call's set-up on this device
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(4):
+        _without_allocation(lib, xs, outs, scales)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    _check_same(lib, xs, outs, scales)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
