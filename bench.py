@@ -2,10 +2,10 @@
 """Benchmark of the B200 FP8 attention hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cosmos]
-                    [--impl b200|reference] [--scaling weak|strong]
+                    [--impl b200|reference] [--scaling strong|weak]
 
 One *step* is one pass of the hot path over one batch: quantize Q, K, V
-(bf16 -> e4m3 + scales) and run the FP8 attention kernel (bf16 out) — the
+(bf16 -> e4m3 + scales) and run the FP8 attention kernel (bf16 out) -- the
 work of the reference's ``fp8_flash_attention`` call.  Default workload: the
 Cosmos-shaped attention (B=2, H=32, S=57600, D=128, N(0,0.5), per-128-token
 block scales).  Metric: algorithmic TFLOP/s (4*B*H*Sq*Skv*D per call), whole
@@ -13,16 +13,28 @@ job aggregate over N GPUs, device-timed with CUDA events, max over ranks.
 
 Multi-GPU (one process per GPU under torchrun):
   cosmos / cfg2  batch x head slices shard across ranks with no collective;
-                 weak scaling by default (every rank a full call's worth of
-                 slices), --scaling strong splits one call's slices.
+                 strong scaling by default (the ranks split one call's
+                 slices, so ``value`` is one call's rate); --scaling weak
+                 gives every rank a full call's worth of slices.  At N > 1
+                 the line also carries a ``wan_cp`` record: the Wan-shaped
+                 call over the same N ranks with context parallelism (NCCL
+                 all-gather of e4m3 K/V), beside rank 0's single-GPU time for
+                 the whole call and a bit-exactness check of sampled slices.
   wan            context parallelism: the sequence splits across ranks, e4m3
                  K/V is all-gathered over NCCL (strong scaling).
   decode         shared-prefix candidate decode, independent replicas.
 
-``--impl reference`` times the reference's own CPU attention (its AMX BF16
-flash kernel, built from its source into oracle/_ref; the numpy oracle when
-that cannot run) on a bounded sample of the same workload on the host cores;
-under torchrun only rank 0 runs it.  Rank 0 prints one JSON line.
+At N = 1 the line carries side records measured outside the timed region:
+the quantize kernel's bandwidth, the shared-prefix decode (CUDA-graph
+replays), torch's bf16 SDPA and the reference's own FP8 Triton kernel on the
+same inputs, and the FP8 linears.
+
+``--impl reference`` times the reference's own CPU attention on a bounded
+sample of the same workload on all the host cores: its default CPU op
+(``AMXSDPAAttention``, torch SDPA on CPU) and its AMX BF16 flash kernel
+(built from its source into oracle/_ref; the numpy oracle when neither can
+run), the faster of the two as ``value``; under torchrun only rank 0 runs it.
+Rank 0 prints one JSON line.
 """
 
 from __future__ import annotations
@@ -171,63 +183,121 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- CPU baseline
-def cpu_reference_sample(w: dict, target_s: float = 8.0) -> dict:
+REF_PKG = REPO / "baseline" / "_ref"  # the reference's package, installed by oracle/build_ref.py
+
+
+def host_cores() -> int:
+    """Host threads this process may run on (its CPU affinity)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def use_all_host_cores() -> int:
+    """Let torch and OpenMP use every host core this process may run on,
+    whatever a launcher exported (torch.distributed.run sets
+    OMP_NUM_THREADS=1).  Call before the reference's OpenMP kernel is loaded:
+    its OpenMP runtime reads OMP_NUM_THREADS when it starts."""
+    n = host_cores()
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    import torch
+
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def reference_cpu_op():  # type: ignore[no-untyped-def]
+    """The reference's default CPU attention op, ``AMXSDPAAttention``
+    (src/repercep/attention/amx_sdpa.py:76-94, which CPUBackend.attention_op
+    picks, src/repercep/backend/cpu.py:281-284), imported unmodified from the
+    installed reference package; None when it is not installed."""
+    if not (REF_PKG / "repercep" / "__init__.py").exists():
+        return None
+    if str(REF_PKG) not in sys.path:
+        sys.path.append(str(REF_PKG))
+    try:
+        from repercep.attention.amx_sdpa import AMXSDPAAttention
+
+        op = AMXSDPAAttention()
+        return op if op.available else None
+    except Exception:
+        return None
+
+
+def _time_calls(fn, target_s: float) -> tuple[float, int]:  # type: ignore[no-untyped-def]
+    """Seconds per call of fn (one warm call, then enough for ~target_s)."""
+    fn()
+    t0 = time.perf_counter()
+    fn()
+    one = time.perf_counter() - t0
+    reps = max(1, min(20, int(target_s / max(one, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return (time.perf_counter() - t0) / reps, reps
+
+
+def cpu_reference_sample(w: dict, target_s: float = 8.0, only: str | None = None) -> dict:
     """Time the reference's CPU attention on a bounded sample of workload `w`.
 
     The reference's CPU path is bf16 (it has no FP8; src/repercep/backend/cpu.py:264).
-    Kind "reference": its AMX flash kernel (kernels/cpu/amx_attn/flash_attn_amx.cpp,
-    built into oracle/_ref) on one (b,h) slice at the full sequence length (the
-    whole problem for the plumbing case).  Kind "port": the numpy oracle on a few
-    query rows of one slice.  Decode: the prefix+suffix attention of one head.
+    Kind "reference": its two CPU ops on one (b,h) slice at the full sequence
+    length (the whole problem for the plumbing case), on all host cores:
+    the default op AMXSDPAAttention (torch SDPA on CPU) and the AMX flash
+    kernel (kernels/cpu/amx_attn/flash_attn_amx.cpp, built into oracle/_ref);
+    ``value`` is the faster one.  Kind "port": the numpy oracle on a few query
+    rows of one slice, when neither reference op can run.  Decode: the
+    prefix+suffix attention of one head.  ``only`` times just the named op.
     """
     import torch
 
     from oracle.build_ref import load_reference_kernel
 
+    cores = use_all_host_cores()
     g = torch.Generator().manual_seed(7)
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     if w["kind"] == "decode":
-        S, D, bh, label = w["P"] + w["C"] * w["T"], w["D"], 1, "one head of the decode (prefix+suffix keys)"
-        flops = flops_per_call(w) / w["H"]
+        S, D, label = w["P"] + w["C"] * w["T"], w["D"], "one head of the decode (prefix+suffix keys)"
+        B, H = 1, 1
     else:
-        D = w["D"]
-        S = w["S"]
-        bh = w["B"] * w["H"] if w["kind"] == "cpu" else 1
-        flops = 4.0 * bh * S * S * D
-        label = "the whole call" if bh > 1 else f"1 (b,h) slice of {w['B'] * w['H']}"
+        D, S = w["D"], w["S"]
+        B, H = (w["B"], w["H"]) if w["kind"] == "cpu" else (1, 1)
+        label = "the whole call" if B * H > 1 else f"1 (b,h) slice of {w['B'] * w['H']}"
+    sm = 1.0 / math.sqrt(D)
+    ops: dict = {}
+    sdpa = reference_cpu_op() if only in (None, "amx-sdpa") else None
+    if sdpa is not None:
+        q, k, v = (torch.randn((B, H, S, D), generator=g).to(torch.bfloat16) for _ in range(3))
+        dt, reps = _time_calls(lambda: sdpa(q, k, v, scale=sm), target_s / 2)
+        ops["amx-sdpa"] = {"value": 4.0 * B * H * S * S * D / dt / 1e12, "S": S,
+                           "desc": f"reference AMXSDPAAttention (its default CPU op): {reps} calls of "
+                                   f"{dt * 1e3:.1f} ms"}
     mod = None
     try:
-        mod = load_reference_kernel()
+        mod = load_reference_kernel() if only in (None, "amx-bf16-flash") else None
     except Exception:
         mod = None
     # The AMX kernel takes sequence lengths in whole 32-row tiles: a ragged S
     # (Wan's 75600) is timed at the multiple of 32 below it; the metric is a rate.
     S_amx = S - S % 32
     if mod is not None and S_amx >= 32 and D in (64, 128):
-        trimmed = S_amx != S
-        S = S_amx
-        B, H = (w["B"], w["H"]) if w["kind"] == "cpu" else (1, 1)
-        q, k, v = (torch.randn((B, H, S, D), generator=g).to(torch.bfloat16) for _ in range(3))
-        sm = 1.0 / math.sqrt(D)
-        mod.flash_attn_bf16(q, k, v, sm, False)
-        t0 = time.perf_counter()
-        mod.flash_attn_bf16(q, k, v, sm, False)
-        one = time.perf_counter() - t0
-        reps = max(1, min(20, int(target_s / max(one, 1e-3))))
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            mod.flash_attn_bf16(q, k, v, sm, False)
-        dt = (time.perf_counter() - t0) / reps
-        flops_sample = 4.0 * B * H * S * S * D
+        q, k, v = (torch.randn((B, H, S_amx, D), generator=g).to(torch.bfloat16) for _ in range(3))
+        dt, reps = _time_calls(lambda: mod.flash_attn_bf16(q, k, v, sm, False), target_s / 2)
+        ops["amx-bf16-flash"] = {
+            "value": 4.0 * B * H * S_amx * S_amx * D / dt / 1e12, "S": S_amx,
+            "desc": f"reference AMX bf16 flash kernel (kernels/cpu/amx_attn): {reps} calls of "
+                    f"{dt * 1e3:.1f} ms" + (" at S rounded down to its 32-row tiles" if S_amx != S else "")}
+    if ops:
+        best = max(ops, key=lambda n: ops[n]["value"])
         return {
-            "value": flops_sample / dt / 1e12,
+            "value": ops[best]["value"],
             "unit": UNIT,
             "cores": cores,
             "kind": "reference",
-            "sample": f"reference AMX bf16 flash kernel (kernels/cpu/amx_attn), {label} at S={S}"
-                      + (" (the workload's S rounded down to the kernel's 32-row tiles)" if trimmed else "")
-                      + f", D={D}: {reps} calls of {dt * 1e3:.1f} ms",
-            "seconds_per_sample": dt,
+            "sample": f"{label} at S={S}, D={D}, bf16, {cores} threads; faster of the reference's CPU ops: "
+                      + "; ".join(f"{n} {o['value']:.3f} TFLOP/s ({o['desc']})" for n, o in ops.items()),
+            "ops": {n: o["value"] for n, o in ops.items()},
+            "best_op": best,
         }
     import numpy as np
 
@@ -244,10 +314,9 @@ def cpu_reference_sample(w: dict, target_s: float = 8.0) -> dict:
     return {
         "value": 4.0 * rows * S * D / dt / 1e12,
         "unit": UNIT,
-        "cores": torch.get_num_threads(),
+        "cores": cores,
         "kind": "port",
         "sample": f"numpy oracle attention, {rows} query rows x {S} keys of one slice",
-        "seconds_per_sample": dt,
     }
 
 
@@ -283,10 +352,11 @@ def parallel_mode(args, w: dict, world: int) -> str:
 def run_reference_arm(args, w: dict, rank: int, world: int) -> None:
     if rank != 0:
         return
+    use_all_host_cores()
     base = cpu_reference_sample(w, target_s=2.0)
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_reference_sample(w, target_s=0.0)
+        r = cpu_reference_sample(w, target_s=0.0, only=base.get("best_op"))
         if i >= args.warmup:
             vals.append(r["value"])
     value = statistics.mean(vals) if vals else base["value"]
@@ -296,7 +366,8 @@ def run_reference_arm(args, w: dict, rank: int, world: int) -> None:
         "warmup": args.warmup, "ms_per_step": ms_call, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "impl": "reference", "config": config_for(args, w, world),
-        "cpu_baseline": {k: base[k] for k in ("unit", "cores", "kind", "sample")} | {"value": value},
+        "cpu_baseline": {k: base[k] for k in ("unit", "cores", "kind", "sample")} | {"value": value}
+                        | ({"ops": base["ops"], "best_op": base["best_op"]} if "ops" in base else {}),
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
         "note": "each step times one bounded sample on the host cores; ms_per_step is the "
@@ -504,6 +575,64 @@ def linear_measurements(dev, stream, peaks: dict) -> dict:  # type: ignore[no-un
             "peak": peak, "peak_source": src, "shapes": rows}
 
 
+def reference_triton_child(workload: str) -> None:
+    """Child-process body of reference_triton_row: the reference's own FP8
+    Triton kernel (kernels/triton_kernels/fp8_flash_attn_hopper.py:432-586,
+    imported unmodified from the installed reference package, static fallback
+    tile because autotuning is disabled) on the workload's rank-0 inputs,
+    beside this package's kernel in the reference's per-(b,h) scale mode on
+    the same inputs.  Prints one JSON line."""
+    import torch
+
+    from triton_kernels.fp8_flash_attn_hopper import fp8_flash_attention  # type: ignore[import-not-found]
+
+    from repercep_runtime_b200 import ops
+
+    w = WORKLOADS[workload]
+    q, k, v = (gen_tensor((w["B"], w["H"], w["S"], w["D"]), w["dist"], i, "cuda:0") for i in range(3))
+    stream = torch.cuda.current_stream()
+    res: dict = {"config": "static fallback tile (REPERCEP_FP8_DISABLE_AUTOTUNE=1)"}
+    t0 = time.perf_counter()
+    out_ref = fp8_flash_attention(q, k, v)
+    torch.cuda.synchronize()
+    res["first_call_s"] = time.perf_counter() - t0
+    ms = _event_ms(lambda: fp8_flash_attention(q, k, v), stream, 3)
+    res["ms"] = ms
+    res["tflops"] = flops_per_call(w) / (ms / 1e3) / 1e12
+    ours = ops.fp8_attention(q, k, v, scale_mode=ops.SCALE_PER_BH)
+    a, b = out_ref.float().flatten(), ours.float().flatten()
+    res["vs_b200_per_bh"] = {
+        "max_abs": float((a - b).abs().max()),
+        "cos": float(torch.nn.functional.cosine_similarity(a, b, dim=0)),
+        "finite": bool(torch.isfinite(a).all()),
+    }
+    print(json.dumps(res), flush=True)
+
+
+def reference_triton_row(workload: str) -> dict:
+    """Run reference_triton_child in a fresh process (a compile or launch
+    failure of the reference's kernel on sm_100 is recorded, never raised)."""
+    if not (REF_PKG / "triton_kernels" / "fp8_flash_attn_hopper.py").exists():
+        return {"unavailable": "the reference package is not installed into baseline/_ref "
+                               "(oracle/build_ref.py needs the reference source tree)"}
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([str(REF_PKG), str(REPO), env.get("PYTHONPATH", "")])
+    env["REPERCEP_FP8_DISABLE_AUTOTUNE"] = "1"
+    code = f"import bench; bench.reference_triton_child({workload!r})"
+    try:
+        proc = subprocess.run([sys.executable, "-c", code], env=env, cwd=str(REPO), capture_output=True,
+                              text=True, timeout=600)
+    except subprocess.TimeoutExpired:
+        return {"failed": "did not finish within 600 s"}
+    if proc.returncode != 0:
+        tail = (proc.stderr or proc.stdout).strip().splitlines()[-3:]
+        return {"failed": f"exit {proc.returncode}: " + " | ".join(tail)[:400]}
+    try:
+        return json.loads(proc.stdout.strip().splitlines()[-1])
+    except (ValueError, IndexError):
+        return {"failed": "no result line: " + proc.stdout[-300:]}
+
+
 def side_measurements(runner: Runner, dev, stream, peaks: dict) -> dict:  # type: ignore[no-untyped-def]
     """Outside the timed region, one GPU only: the quantize kernel's bandwidth
     and torch's bf16 SDPA on the same inputs (the GPU comparison rows)."""
@@ -543,10 +672,8 @@ def side_measurements(runner: Runner, dev, stream, peaks: dict) -> dict:  # type
             rows[name] = {"ms": ms, "tflops": runner.rank_flops / (ms / 1e3) / 1e12}
         except Exception as e:  # backend not available for this shape / build
             rows[name] = {"unavailable": f"{type(e).__name__}: {str(e)[:120]}"}
-    rows["reference_fp8_triton"] = {"unavailable": "the reference's Triton FP8 kernel lives in its "
-                                    "kernels/triton_kernels tree, outside its installable package "
-                                    "(src/repercep), so nothing of it reaches the GPU box; its CPU "
-                                    "path is the --impl reference arm"}
+    if os.environ.get("REPERCEP_BENCH_REF_TRITON", "1") != "0":
+        rows["reference_fp8_triton"] = reference_triton_row(runner.args.workload)
     out["gpu_comparison"] = rows
     torch.cuda.synchronize(dev)
     try:
@@ -578,6 +705,146 @@ def dominant_roofline(w: dict, runner: Runner, kernel_ms: float, peaks: dict) ->
     return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
             "traffic": profile_traffic(runner.args.workload), "peak_source": src,
             "kernel": "fa8_fwd_kernel<2,%d>" % runner.args.p_mode}
+
+
+def decode_record(args, dev, stream, peaks: dict) -> dict:  # type: ignore[no-untyped-def]
+    """The shared-prefix decode (token-VLA config) on this GPU, outside the
+    timed region: one decode step (quantize the new queries and suffix K/V,
+    then the decode kernel) and the kernel alone, each captured once as a
+    CUDA graph and replayed, timed per replay with CUDA events."""
+    import torch
+
+    w = WORKLOADS["decode"]
+    r = Runner(args, w, 0, 1, dev)
+    for _ in range(3):
+        r.step()
+    g_step, g_kernel = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        r.step()
+    qq, kx, vx = r.quantized_suffix()
+    with torch.cuda.graph(g_kernel):
+        r.decode_kernel(qq, kx, vx)
+    n = 50
+    out = {}
+    for name, g in (("step_us", g_step), ("kernel_us", g_kernel)):
+        for _ in range(5):
+            g.replay()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for a, b in evs:
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        out[name] = 1e3 * statistics.median(a.elapsed_time(b) for a, b in evs)
+    roof = dominant_roofline(w, r, out["kernel_us"] / 1e3, peaks)
+    del g_step, g_kernel
+    return {"workload": "decode", "desc": w["desc"], **out,
+            "tflops": flops_per_call(w) / (out["kernel_us"] / 1e6) / 1e12,
+            "achieved_gbs": roof["achieved"], "peak_gbs": roof["peak"], "frac": roof["frac"],
+            "algorithmic_bytes": roof["algorithmic_bytes"], "kernel": roof["kernel"],
+            "timing": f"median of {n} CUDA-graph replays, each bracketed by CUDA events"}
+
+
+def wan_cp_record(args, rank: int, world: int, dev, stream) -> dict | None:  # type: ignore[no-untyped-def]
+    """The Wan-shaped call (B2 H40 S75600) over this job's ranks with context
+    parallelism, beside rank 0's single-GPU time for the whole call on the
+    same box, and a bit-exactness check of sampled (b,h) slices against it.
+
+    Every rank builds the same global inputs from one seed and attends its
+    shard of the sequence (ContextParallelAttention: per-block quantize, NCCL
+    all-gather of e4m3 K/V and scales into this GPU's memory, chunked
+    attention overlapped with the gathers).  Times are CUDA events, max over
+    ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from repercep_runtime_b200 import ops
+    from repercep_runtime_b200.parallel import CP_CHUNKS, ContextParallelAttention, nccl_all_gather
+
+    w = WORKLOADS["wan"]
+    B, H, S, D = w["B"], w["H"], w["S"], w["D"]
+    d = str(dev)
+    full = [gen_tensor((B, H, S, D), w["dist"], 900 + i, d) for i in range(3)]
+    cp = ContextParallelAttention(S, rank, world, all_gather=nccl_all_gather(), p_mode=args.p_mode)
+    sh = cp.shard
+    q, k, v = (x[:, :, sh.start:sh.start + sh.rows].contiguous() for x in full)
+
+    def timed(fn, n: int) -> float:  # type: ignore[no-untyped-def]
+        fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([a.elapsed_time(b) / n], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    out_cp = cp(q, k, v)
+    cp_ms = timed(lambda: cp(q, k, v, out=out_cp), 5)
+    quant_ms = timed(lambda: ops.quantize_fp8((q, k, v), scale_mode=ops.SCALE_PER_BLOCK128), 5)
+    qq, kq, vq = ops.quantize_fp8((q, k, v), scale_mode=ops.SCALE_PER_BLOCK128)
+    bh = B * H
+    k_all, v_all, ks_all, vs_all = cp.gather_kv(kq.data.view(torch.uint8).reshape(bh, sh.rows, D),
+                                                 vq.data.view(torch.uint8).reshape(bh, sh.rows, D),
+                                                 kq.scales, vq.scales)
+    attn_out = torch.empty_like(out_cp)
+    attn_ms = timed(lambda: ops.attention_fp8_chunked(
+        qq, k_all.view(ops.FP8), v_all.view(ops.FP8), ks_all, vs_all, last_rows=sh.last_rows,
+        p_mode=args.p_mode, out=attn_out), 5)
+    del k_all, v_all, attn_out
+
+    # rank 0: the whole call on one GPU (the other ranks wait at the barrier)
+    single_ms, out1 = None, None
+    if rank == 0:
+        def one():  # type: ignore[no-untyped-def]
+            a8, b8, c8 = ops.quantize_fp8(full, scale_mode=ops.SCALE_PER_BLOCK128)
+            return ops.attention_fp8_quantized(a8, b8, c8, p_mode=args.p_mode)
+
+        out1 = one()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(3):
+            one()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        single_ms = a.elapsed_time(b) / 3
+    dist.barrier()
+
+    # bit-exactness: sampled (b,h) slices of every rank's rows, gathered to all ranks
+    samples = sorted({0, bh // 2, bh - 1})
+    mine = torch.zeros((len(samples), sh.chunk_rows, D), dtype=out_cp.dtype, device=dev)
+    o3 = out_cp.reshape(bh, sh.rows, D)
+    for i, s_ in enumerate(samples):
+        mine[i, :sh.rows].copy_(o3[s_])
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine)
+    record = None
+    if rank == 0:
+        got = torch.cat(parts, dim=1)[:, :S]
+        ref = out1.reshape(bh, S, D)[samples]
+        exact = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+        fl = flops_per_call(w)
+        record = {
+            "workload": "wan", "desc": w["desc"], "n_gpus": world,
+            "parallelism": f"context-parallel x{world} (NCCL all-gather of e4m3 K/V + scales, "
+                           f"{CP_CHUNKS} overlapped (b,h) chunks)",
+            "ms_per_call": cp_ms, "tflops": fl / (cp_ms / 1e3) / 1e12,
+            "tflops_per_gpu": fl / (cp_ms / 1e3) / 1e12 / world,
+            "quantize_ms": quant_ms, "attention_ms": attn_ms,
+            "exposed_gather_ms": cp_ms - quant_ms - attn_ms,
+            "single_gpu_ms_rank0": single_ms, "single_gpu_tflops_rank0": fl / (single_ms / 1e3) / 1e12,
+            "bit_exact_vs_single_gpu": exact, "sampled_bh_slices": samples,
+            "timing": "CUDA events over 5 calls after a warm call, max over ranks; single GPU: rank 0 "
+                      "alone, 3 calls",
+        }
+    del full, q, k, v, out_cp, qq, kq, vq, out1, mine, parts
+    torch.cuda.empty_cache()
+    return record
 
 
 def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
@@ -651,6 +918,11 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     value = runner.job_flops * args.steps / (ms_total / 1e3) / 1e12
 
     side = side_measurements(runner, dev, stream, load_peaks()) if world == 1 and not args.no_side else {}
+    if world == 1 and not args.no_side and w["kind"] != "decode":
+        try:
+            side["decode"] = decode_record(args, dev, stream, load_peaks())
+        except Exception as e:  # a failure here must not hide the headline line
+            side["decode"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
 
     e2e = None
     if not args.no_e2e:
@@ -700,19 +972,24 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             "api": api,
         }
 
+    wan_cp = None
+    if world > 1 and w["kind"] == "attn" and runner.mode != "cp" and not args.no_wan_cp:
+        del runner.inputs  # this rank's Cosmos slices are no longer needed
+        torch.cuda.empty_cache()
+        wan_cp = wan_cp_record(args, rank, world, dev, stream)
+
     if rank != 0:
         return
     peaks = load_peaks()
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         r = cpu_reference_sample(w)
-        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "ops", "best_op") if k in r}
     per_gpu = value / world
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "strong" if (runner.mode == "cp" or (runner.mode == "shard" and args.scaling == "strong"))
-        else "weak",
+        "scaling": "weak" if w["kind"] == "decode" else ("strong" if runner.mode == "cp" else args.scaling),
         "vs_baseline": None, "dtype": "fp8_e4m3", "data": "synthetic",
         "config": config_for(args, w, world),
         "tflops_per_gpu": per_gpu,
@@ -730,6 +1007,8 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
         "cuda_graph": graphs is not None,
         "device_status": status,
     }
+    if wan_cp is not None:
+        line["wan_cp"] = wan_cp
     print(json.dumps(line), flush=True)
 
 
@@ -740,13 +1019,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cosmos")
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--scaling", choices=("weak", "strong"), default="weak")
+    ap.add_argument("--scaling", choices=("weak", "strong"), default="strong")
     ap.add_argument("--p-mode", type=int, choices=(0, 1), default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the side measurements (quantize bandwidth, SDPA and FP8 linear rows)")
     ap.add_argument("--no-graph", action="store_true", help="decode: launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--no-wan-cp", action="store_true", help="N > 1: skip the wan_cp record")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
