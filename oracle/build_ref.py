@@ -105,7 +105,13 @@ def install_reference_package(reference: Path) -> Path | None:
         dst = REF_PKG_DIR / name
         if dst.exists():
             shutil.rmtree(dst)
-        shutil.copytree(src_dir, dst, ignore=shutil.ignore_patterns("__pycache__", "*.pyc"))
+        # plain file copies (no permission bits): the installed tree stays
+        # writable, so Python can cache bytecode and a later install can replace it
+        shutil.copytree(src_dir, dst, ignore=shutil.ignore_patterns("__pycache__", "*.pyc"),
+                        copy_function=shutil.copyfile)
+        for d in [dst, *dst.rglob("*")]:
+            if d.is_dir():
+                d.chmod(0o755)
     return REF_PKG_DIR
 
 

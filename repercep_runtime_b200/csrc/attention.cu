@@ -44,6 +44,7 @@ constexpr int kDefaultExpPoly = 2;
 constexpr int kDefaultRowSplit = 1;
 constexpr float kDefaultRescaleTau = 1.0f;
 constexpr int kDefaultStagger = 2;
+constexpr int kDefaultMmaAhead = 0;
 
 // Pipeline tracing (compiled in only with -DRP_PIPELINE_TRACE): one chosen CTA
 // records (SM clock, event << 16 | step) at every barrier hand-off of every
@@ -119,14 +120,14 @@ struct Cfg {
   static constexpr int kTableSteps = TAB ? ((NSPLIT == 2) ? 1536 : 2048) : 0;
   static constexpr int kTabBytes = TAB ? 64 + kTableSteps * 16 : 0;
   static constexpr int kOffBar = kOffT + kTabBytes;
-  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ + 8;
+  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ + 32;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Bars {
   uint64_t *q_full, *k_full, *k_empty, *v_full, *v_empty;
-  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *xch, *stag;
+  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *xch, *stag, *stag1;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -148,8 +149,9 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   b.epi = b.o_final + NQ;
   b.fin = b.epi + NQ;
   b.xch = b.fin + 1;  // [NQ][4 lane quarters][3]: row-max (x2 by step parity), row-sum
-  b.stag = b.xch + 12 * NQ;  // [4 lane quarters][2 by step parity]: tile 0 exp done
-  b.tmem_slot = reinterpret_cast<uint32_t*>(b.stag + 8);
+  b.stag = b.xch + 12 * NQ;  // [4 lane quarters][4 by step mod 4]: tile 0 exp done
+  b.stag1 = b.stag + 16;     // [4 lane quarters][4 by step mod 4]: tile 1 exp done
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.stag1 + 16);
   b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
   return b;
 }
@@ -471,6 +473,102 @@ __device__ void mma_issuer(const AttnKernelParams& p, const Bars& bar, uint8_t* 
   mbar_drain(bar.fin, 0);
 }
 
+// MMA issue order "ahead" (not the decode): S of steps 0 and 1 for every tile
+// first; then, for each step i, for each tile t: PV_t(i) (waits for P_t(i)),
+// then QK_t(i + 2) (waits for the softmax to have loaded S_t(i + 1)).  Each
+// tile thus has its next S computed while its softmax works on the current
+// step, and a tile's QK never waits behind another tile's P.  The tensor pipe
+// runs in order, so S_full_t(i + 2) still implies PV_t(i) is done: P buffer
+// i & 1 is free again when the softmax writes P_t(i + 2) there.
+template <int NQ, int PMODE, int DB>
+__device__ void mma_issuer_ahead(const AttnKernelParams& p, const Bars& bar, uint8_t* smem,
+                                 uint32_t tmem, int n_steps) {
+  using C = Cfg<NQ, PMODE, 1, false, DB>;
+  constexpr uint32_t idesc_qk = make_idesc_e4m3(128, 128, 0, 0);
+  constexpr uint32_t idesc_pv = make_idesc_e4m3(128, 128, 0, 1);
+  const uint32_t sbase = smem_u32(smem);
+  auto wait_k = [&](int j) -> bool {
+    return mbar_wait(bar.k_full + j % C::kSt, (j / C::kSt) & 1, bar.abort_flag, p.status, kErrWaitK);
+  };
+  // S_t = Q_t K(j)^T, once the softmax has loaded S_t of step j - 1.
+  auto qk = [&](int j, int t) -> bool {
+    if (j > 0 &&
+        !mbar_wait(bar.s_free + t, (j - 1) & 1, bar.abort_flag, p.status, kErrWaitSFree))
+      return false;
+    tc_fence_after();
+    const int ks = j % C::kSt;
+#pragma unroll
+    for (int kb = 0; kb < DB; ++kb) {
+      const uint64_t kd =
+          make_sw128_desc(sbase + C::kOffK + ks * C::kKVBytes + kb * kTileBytes, 16, 1024);
+      const uint64_t qd = make_sw128_desc(sbase + C::kOffQ + t * C::kQBytes + kb * kTileBytes, 16, 1024);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma_f8(tmem + t * kTile, qd + 2 * k, kd + 2 * k, idesc_qk, (kb > 0 || k > 0) ? 1u : 0u);
+    }
+    mma_commit(bar.s_full + t);
+    return true;
+  };
+  bool ok = mbar_wait(bar.q_full, 0, bar.abort_flag, p.status, kErrWaitQ);
+  for (int j = 0; ok && j < n_steps && j < 2; ++j) {
+    ok = wait_k(j);
+    for (int t = 0; ok && t < NQ; ++t) ok = qk(j, t);
+    if (ok) mma_commit(bar.k_empty + j % C::kSt);
+  }
+  for (int i = 0; ok && i < n_steps; ++i) {
+    const int vsl = i % C::kSt;
+    if (!mbar_wait(bar.v_full + vsl, (i / C::kSt) & 1, bar.abort_flag, p.status, kErrWaitV)) {
+      ok = false;
+      break;
+    }
+    const bool more = i + 2 < n_steps;
+#pragma unroll
+    for (int t = 0; t < NQ; ++t) {
+      if (!mbar_wait(bar.p_full + 2 * t + (i & 1), (i >> 1) & 1, bar.abort_flag, p.status,
+                     kErrWaitP)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int pb = (C::kPBuf == 2) ? (i & 1) : 0;
+      const uint32_t paddr = sbase + C::kOffP + (t * C::kPBuf + pb) * C::kPStride;
+      const uint64_t pd = make_sw128_desc(paddr, 16, 1024);
+#pragma unroll
+      for (int nb = 0; nb < DB; ++nb) {
+        const uint64_t vd = make_sw128_desc(
+            sbase + C::kOffV + vsl * C::kKVBytes + nb * kTileBytes, kTileBytes, 1024);
+        const uint32_t d_tmem = tmem + (NQ + t * DB + nb) * kTile;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_f8(d_tmem, pd + 2 * k, vd + 256 * k, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+        if constexpr (PMODE == 1) {
+          const uint64_t pl = make_sw128_desc(paddr + kTileBytes, 16, 1024);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_f8(d_tmem, pl + 2 * k, vd + 256 * k, idesc_pv, 1u);
+        }
+      }
+      mma_commit(bar.o_done + t);
+      if (i == n_steps - 1) mma_commit(bar.o_final + t);
+      if (more) {
+        if (t == 0 && !wait_k(i + 2)) {
+          ok = false;
+          break;
+        }
+        if (!qk(i + 2, t)) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) break;
+    mma_commit(bar.v_empty + vsl);
+    if (more) mma_commit(bar.k_empty + (i + 2) % C::kSt);
+  }
+  // Everything this thread issued must finish before TMEM is released.
+  mma_commit(bar.fin);
+  mbar_drain(bar.fin, 0);
+}
+
 // ----------------------------------------------------------------- softmax
 // NSPLIT threads share each query row: thread (half, row) owns S columns
 // [half * kNC, half * kNC + kNC).  With NSPLIT = 2 the two halves swap their
@@ -700,13 +798,22 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
 
     // Stagger: tile 1's exp phase starts after tile 0's of the same step, so
     // the two warps sharing an SM sub-partition alternate MUFU-bound and
-    // latency-bound phases.  Tile 0 is never two steps ahead here (its S for
-    // step j+2 is issued only after tile 1's P of step j), so the barrier
-    // pair indexed by step parity is never two phases ahead.
+    // latency-bound phases.  Tile 0 is at most two steps ahead of tile 1 (its
+    // S for step j+3 is issued only after tile 1's P of step j, in either MMA
+    // order), so four barriers indexed by step mod 4 never run a phase ahead
+    // of their waiter.
+    // Stagger 3 (ping-pong) also holds tile 0's exp phase of step j until
+    // tile 1's of step j - 1 is done, so the two never overlap.
     const bool stag_step =
-        !KS && NQ == 2 && NSPLIT == 1 && (p.stagger == 2 || (p.stagger == 1 && j == 0));
+        !KS && NQ == 2 && NSPLIT == 1 && (p.stagger >= 2 || (p.stagger == 1 && j == 0));
     if (stag_step && t == 1 &&
-        !warp_wait(bar.stag + 2 * wq + (j & 1), (j >> 1) & 1, bar.abort_flag, p.status, kErrWaitStag)) {
+        !warp_wait(bar.stag + 4 * wq + (j & 3), (j >> 2) & 1, bar.abort_flag, p.status, kErrWaitStag)) {
+      ok = false;
+      break;
+    }
+    if (stag_step && p.stagger == 3 && t == 0 && j > 0 &&
+        !warp_wait(bar.stag1 + 4 * wq + ((j - 1) & 3), ((j - 1) >> 2) & 1, bar.abort_flag, p.status,
+                   kErrWaitStag)) {
       ok = false;
       break;
     }
@@ -743,7 +850,11 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     if (tracer) RP_TRACE(108 + t, j);
     if (stag_step && t == 0) {
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar.stag + 2 * wq + (j & 1));
+      if (lane == 0) mbar_arrive(bar.stag + 4 * wq + (j & 3));
+    }
+    if (stag_step && p.stagger == 3 && t == 1) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar.stag1 + 4 * wq + (j & 3));
     }
     // Next step's constants (their MUFU ops queue behind this step's exps and
     // are consumed a whole step later), then the scale loads for step j+2.
@@ -994,7 +1105,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
     }
     mbar_init(bar.fin, 1);
     for (int i = 0; i < 12 * NQ; ++i) mbar_init(bar.xch + i, 2);
-    for (int i = 0; i < 8; ++i) mbar_init(bar.stag + i, 1);
+    for (int i = 0; i < 32; ++i) mbar_init(bar.stag + i, 1);
     *bar.abort_flag = 0;
     fence_barrier_init();
   }
@@ -1025,7 +1136,12 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
     if (lane == 0)
       producer<NQ, PMODE, DB, KS>(&tm_q, &tm_k, &tm_v, &tm_kx, &tm_vx, p, bar, smem, n_steps);
   } else if (warp == C::kMmaWarp) {
-    if (lane == 0) mma_issuer<NQ, PMODE, DB, KS>(p, bar, smem, tmem, n_steps);
+    if (lane == 0) {
+      if (!KS && p.mma_ahead)
+        mma_issuer_ahead<NQ, PMODE, DB>(p, bar, smem, tmem, n_steps);
+      else
+        mma_issuer<NQ, PMODE, DB, KS>(p, bar, smem, tmem, n_steps);
+    }
   } else {
     softmax_wg<NQ, PMODE, EPOLY, NSPLIT, TAB, DB, KS>(&tm_o, p, bar, smem, tmem, n_steps);
   }
@@ -1142,14 +1258,27 @@ int split_setting() {
   return v;
 }
 
-// Exp-phase stagger of the two query tiles (0, 1 or 2).
+// Exp-phase stagger of the two query tiles (0 off, 1 first step only, 2 tile 1
+// after tile 0 every step, 3 ping-pong: also tile 0 after tile 1's previous).
 // REPERCEP_B200_STAGGER overrides the default (read once).
 int stagger_setting() {
   static const int v = [] {
     const char* e = std::getenv("REPERCEP_B200_STAGGER");
     if (!e) return kDefaultStagger;
     const int x = std::atoi(e);
-    return (x >= 0 && x <= 2) ? x : kDefaultStagger;
+    return (x >= 0 && x <= 3) ? x : kDefaultStagger;
+  }();
+  return v;
+}
+
+// MMA issue order of the attention kernel (1: each tile's PV(i) then its
+// QK(i + 2); 0: every tile's QK(j), then every tile's PV(j - 1)).
+// REPERCEP_B200_MMA_AHEAD overrides the default (read once).
+int mma_ahead_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_MMA_AHEAD");
+    if (!e) return kDefaultMmaAhead;
+    return std::atoi(e) != 0 ? 1 : 0;
   }();
   return v;
 }
@@ -1189,6 +1318,7 @@ cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& param
   AttnKernelParams p = params;
   p.rescale_tau = rescale_tau_setting();
   p.stagger = stagger_setting();
+  p.mma_ahead = mma_ahead_setting();
   if (db == 2) {
     if (nq != 1) return cudaErrorInvalidValue;
     return (p_mode == 0) ? launch_variant<1, 0, 2, 1, 2>(maps, p, B, H, st)

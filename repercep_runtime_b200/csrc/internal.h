@@ -101,8 +101,13 @@ struct AttnKernelParams {
   // are rescaled only when some row's max grows by more than this; P is
   // scaled by 2^-rescale_tau so a stale max never saturates e4m3.
   float rescale_tau;
-  // Two-tile exp stagger: 0 off, 1 at the first step only, 2 every step.
+  // Two-tile exp stagger: 0 off, 1 at the first step only, 2 every step, 3
+  // ping-pong (tile 0 also waits for tile 1's exp phase of the previous step).
   int stagger;
+  // MMA issue order (not the decode): 1 = per step i, each tile's PV(i) and
+  // then that tile's QK(i + 2), so a tile's next S never waits behind another
+  // tile's P; 0 = every tile's QK(j), then every tile's PV(j - 1).
+  int mma_ahead;
   int causal;
   // Output: fp16 instead of bf16; out_plain = one unswizzled box of out_cols
   // (32 or 64) columns instead of 64-column swizzled boxes.

@@ -13,7 +13,11 @@ library reads these switches once per process):
 * REPERCEP_B200_DECODE_KSPLIT=0 -- the shared-prefix decode on one softmax
   warpgroup taking every K/V step (instead of two taking alternate steps);
 * REPERCEP_B200_DECODE_PDL=0 -- the decode launched after its quantize launch
-  completes instead of as its programmatic dependent.
+  completes instead of as its programmatic dependent;
+* REPERCEP_B200_MMA_AHEAD=1 -- per step, each tile's PV followed by its
+  next-but-one QK (instead of every tile's QK, then every tile's PV);
+* REPERCEP_B200_STAGGER=3 -- ping-pong: tile 0's exp phase also waits for
+  tile 1's of the previous step.
 """
 
 from __future__ import annotations
@@ -41,6 +45,8 @@ SUITE = ["tests/test_attention_gpu.py", "tests/test_decode_gpu.py", "tests/test_
         "REPERCEP_B200_EXP_POLY=4",
         "REPERCEP_B200_DECODE_KSPLIT=0",
         "REPERCEP_B200_DECODE_PDL=0",
+        "REPERCEP_B200_MMA_AHEAD=1",
+        "REPERCEP_B200_STAGGER=3",
     ],
 )
 def test_attention_suite_under_schedule_switch(switch):
