@@ -570,6 +570,34 @@ def linear_measurements(dev, stream, peaks: dict) -> dict:  # type: ignore[no-un
         row["torch_bf16_tflops"] = fl / ms / 1e9
         rows[name] = row
         del x, w, x8, w8, xs, ws, wt, sa, sb
+    # The QKV projection feeding attention: the per-128-token-block quantizer
+    # fused into the GEMM epilogue (rp_fp8_gemm_qkv_quant) against the GEMM
+    # with a bf16 output followed by the quantize launch it replaces.
+    from repercep_runtime_b200 import ops
+
+    M, K, N = LINEAR_SHAPES["qkv"]
+    H = N // (3 * 128)
+    g = torch.Generator(device=dev).manual_seed(1)
+    x8, xs = linear.quantize_rows(torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16))
+    w8, ws = linear.quantize_rows((torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16))
+    fl = 2.0 * M * N * K
+
+    def separate():  # type: ignore[no-untyped-def]
+        c5 = linear.gemm_ex(x8, w8, xs, ws).view(1, M, 3, H, 128)
+        return ops.quantize_fp8([c5[:, :, i] for i in range(3)], scale_mode=ops.SCALE_PER_BLOCK128,
+                                layout="bshd")
+
+    ms_f = _event_ms(lambda: linear.gemm_qkv_quant(x8, w8, xs, ws, H, M), stream, 10)
+    ms_s = _event_ms(separate, stream, 10)
+    rows["qkv_quant"] = {
+        "M": M, "K": K, "N": N, "heads": H,
+        "fused_ms": ms_f, "separate_ms": ms_s, "fused_tflops": fl / ms_f / 1e9,
+        "separate_tflops": fl / ms_s / 1e9,
+        "bf16_bytes_avoided": 2 * 2 * M * N,
+        "desc": "QKV GEMM -> e4m3 Q/K/V + per-128-token-block scales: fused epilogue vs GEMM (bf16 out) "
+                "then the quantize launch; outputs bit-identical (tests/test_qkv_quant_gpu.py)",
+    }
+    del x8, w8, xs, ws
     torch.cuda.synchronize(dev)
     return {"kernel": "fp8_gemm_kernel (2-SM pairs, 256x256 tiles)", "bound": "tensor", "unit": "TFLOP/s",
             "peak": peak, "peak_source": src, "shapes": rows}

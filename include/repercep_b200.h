@@ -30,6 +30,8 @@
  *                             (bound by fp8_gemm, kernels/hip/fp8_attn/binding.cpp:24-61)
  *   rp_fp8_gemm_ex, rp_quant_fp8_rows <- (no reference kernel: FP8 DiT linears are the
  *                             reference's planned use of that GEMM, docs/OPTIMIZATION.md:161-162)
+ *   rp_fp8_gemm_qkv_quant  <- the QKV projection followed by the eager quantize of Q, K, V,
+ *                             fp8_flash_attn_hopper.py:474-480 (per-128-token-block mode)
  */
 #ifndef REPERCEP_B200_H_
 #define REPERCEP_B200_H_
@@ -41,7 +43,7 @@
 extern "C" {
 #endif
 
-#define RP_ABI_VERSION 3
+#define RP_ABI_VERSION 4
 
 typedef enum rp_status {
   RP_OK = 0,
@@ -225,6 +227,28 @@ int rp_fp8_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, int b
                    const float* sa, int64_t sa_stride, float a_scale, const float* sb,
                    int64_t sb_stride, float b_scale, const void* bias, void* c, int64_t ldc,
                    int out_dtype, int M, int N, int K, void* stream);
+
+/* The QKV projection with the attention quantizer fused into its epilogue.
+ * Replaces the reference's eager quantize of Q, K and V right before its
+ * kernel (kernels/triton_kernels/fp8_flash_attn_hopper.py:474-480) for the
+ * per-128-token-block scale mode: the projection's bf16 output is never
+ * written.
+ *   a      (B*S, K) e4m3 activations, row m at a + m * lda bytes (lda % 16 == 0);
+ *          rows are B batches of S tokens
+ *   w      (N, K) e4m3 weight, N = 3 * H * 128 (the Q, K, V projections
+ *          stacked, each head-major), row n at w + n * ldw bytes (ldw % 16 == 0)
+ *   sa, sa_stride, a_scale, sb, sb_stride, b_scale, bias (bf16 (N,) or NULL)
+ *          as in rp_fp8_gemm_ex
+ *   q8, k8, v8   (B*H, S, 128) e4m3 each (16-byte aligned)
+ *   qs, ks, vs   (B*H, ceil(S/128)) fp32 each
+ * The result is bit for bit what rp_fp8_gemm_ex (bf16 output) followed by
+ * rp_quant_fp8_e4m3 (RP_SCALE_PER_BLOCK128) on the (B, S, 3, H, 128) view of
+ * that output produce. */
+int rp_fp8_gemm_qkv_quant(const void* a, int64_t lda, const void* w, int64_t ldw,
+                          const float* sa, int64_t sa_stride, float a_scale, const float* sb,
+                          int64_t sb_stride, float b_scale, const void* bias, int B, int S,
+                          int H, int K, void* q8, void* k8, void* v8, float* qs, float* ks,
+                          float* vs, void* stream);
 
 /* Row-wise e4m3 quantizer for linear operands: x (rows, cols) bf16 or fp16
  * (in_dtype), row r at x + r * ldx elements (16-byte aligned rows, cols % 8

@@ -159,9 +159,36 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_void_p, ctypes.c_int64, _c_int, _c_int, _c_int, _c_void_p, ctypes.c_int64, _c_void_p, _c_void_p],
     ),
+    "rp_fp8_gemm_qkv_quant": (
+        _c_int,
+        [
+            _c_void_p,
+            ctypes.c_int64,
+            _c_void_p,
+            ctypes.c_int64,
+            _c_void_p,
+            ctypes.c_int64,
+            _c_float,
+            _c_void_p,
+            ctypes.c_int64,
+            _c_float,
+            _c_void_p,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_void_p,
+            _c_void_p,
+            _c_void_p,
+            _c_void_p,
+            _c_void_p,
+            _c_void_p,
+            _c_void_p,
+        ],
+    ),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

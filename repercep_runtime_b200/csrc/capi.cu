@@ -574,6 +574,59 @@ int rp_fp8_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, int b
   return RP_OK;
 }
 
+int rp_fp8_gemm_qkv_quant(const void* a, int64_t lda, const void* w, int64_t ldw,
+                          const float* sa, int64_t sa_stride, float a_scale, const float* sb,
+                          int64_t sb_stride, float b_scale, const void* bias, int B, int S,
+                          int H, int K, void* q8, void* k8, void* v8, float* qs, float* ks,
+                          float* vs, void* stream) {
+  if (B <= 0 || S <= 0 || H <= 0 || K <= 0) return fail(RP_ERR_INVALID, "B, S, H, K must be positive");
+  if ((int64_t)B * H > 65535) return fail(RP_ERR_UNSUPPORTED, "B*H > 65535");
+  const int64_t M = (int64_t)B * S, N = (int64_t)3 * H * 128;
+  if (M > 0x7FFFFFFF || N > 0x7FFFFFFF) return fail(RP_ERR_UNSUPPORTED, "B*S or 3*H*128 too large");
+  if (!a || !w || !q8 || !k8 || !v8 || !qs || !ks || !vs)
+    return fail(RP_ERR_INVALID, "a, w, the three outputs and their scales must be non-null");
+  if (lda < K || ldw < K) return fail(RP_ERR_INVALID, "row pitches are shorter than K");
+  if (lda % 16 != 0 || ldw % 16 != 0)
+    return fail(RP_ERR_ALIGN, "e4m3 row pitches must be multiples of 16 bytes (lda=%lld ldw=%lld)",
+                (long long)lda, (long long)ldw);
+  if (!aligned16(q8) || !aligned16(k8) || !aligned16(v8))
+    return fail(RP_ERR_ALIGN, "q8, k8 and v8 must be 16-byte aligned");
+  if ((sa && sa_stride < 0) || (sb && sb_stride < 0))
+    return fail(RP_ERR_INVALID, "scale strides must be non-negative");
+  int* status = nullptr;
+  int rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+  CUtensorMap ma{}, mb{};
+  if ((rc = make_mat8_map(&ma, a, K, M, lda, 128, "a")) != RP_OK) return rc;
+  if ((rc = make_mat8_map(&mb, w, K, N, ldw, rp::gemm_b_box_rows(true), "w")) != RP_OK) return rc;
+  rp::GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = K;
+  p.group_m = 0;
+  p.sa = sa;
+  p.sa_stride = sa_stride;
+  p.a_scale = a_scale;
+  p.sb = sb;
+  p.sb_stride = sb_stride;
+  p.b_scale = b_scale;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.C = nullptr;
+  p.status = status;
+  p.qkv_S = S;
+  p.qkv_H = H;
+  p.qkv_nblk = (S + 127) / 128;
+  p.qkv_out[0] = static_cast<uint8_t*>(q8);
+  p.qkv_out[1] = static_cast<uint8_t*>(k8);
+  p.qkv_out[2] = static_cast<uint8_t*>(v8);
+  p.qkv_scales[0] = qs;
+  p.qkv_scales[1] = ks;
+  p.qkv_scales[2] = vs;
+  cudaError_t e = rp::launch_fp8_gemm(ma, mb, p, true, false, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 qkv gemm launch");
+  return RP_OK;
+}
+
 int rp_fp8_gemm(const void* a, const void* b, void* c, float a_scale, float b_scale, int M,
                 int N, int K, void* stream) {
   if (K % 16 != 0 || N % 16 != 0)

@@ -43,6 +43,7 @@
 
 #include "internal.h"
 #include "ptx.cuh"
+#include "quant_common.cuh"
 
 namespace rp {
 
@@ -68,7 +69,9 @@ struct GCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;           // 32 / 48 KB
   static constexpr int kStages = PAIR ? 6 : 4;
   static constexpr int kOffCol = kStages * kStageBytes;
-  static constexpr int kOffBar = kOffCol + kColBytes;
+  // fused QKV quantize: per-warp block amax, [2 tile parities][2 halves][4 lane quarters]
+  static constexpr int kOffAmax = kOffCol + kColBytes;
+  static constexpr int kOffBar = kOffAmax + 2 * 2 * 4 * 4;
   static constexpr int kNumBars = 2 * kStages + 2 + 2 + 1;  // full, empty, acc_full, acc_empty, fin
   static constexpr int kSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
   // acc_empty arrivals: every epilogue warp of the pair
@@ -139,6 +142,19 @@ __device__ __forceinline__ int tile_units() {
   return PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 }
 
+// First A row of this CTA's part of row tile cm: tiles in row order, or (fused
+// QKV quantize) per batch -- the tile's rows within its batch of qkv_S tokens,
+// offset by the batch (rows past the batch are masked by the epilogue).
+template <bool PAIR>
+__device__ __forceinline__ int tile_row0(const GemmParams& p, int cm, uint32_t rank) {
+  using C = GCfg<PAIR>;
+  if (p.qkv_S > 0) {
+    const int b = cm / p.qkv_per_b;
+    return b * p.qkv_S + (cm - b * p.qkv_per_b) * C::kTileM + static_cast<int>(rank) * kCtaRows;
+  }
+  return cm * C::kTileM + static_cast<int>(rank) * kCtaRows;
+}
+
 template <bool PAIR>
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const GemmBars& b,
                                          int* status, int code) {
@@ -154,7 +170,7 @@ __device__ void gemm_producer(const CUtensorMap* ta, const CUtensorMap* tb, cons
   bool ok = true;
   for (int t = tile_unit<PAIR>(); ok && t < p.tiles; t += tile_units<PAIR>()) {
     const TileCoord c = tile_coord(p, t);
-    const int m0 = c.m * C::kTileM + static_cast<int>(rank) * kCtaRows;
+    const int m0 = tile_row0<PAIR>(p, c.m, rank);
     const int n0 = c.n * kTileN + static_cast<int>(rank) * C::kBRows;
     for (int kb = 0; kb < p.n_kb; ++kb, ++g) {
       const int s = g % C::kStages;
@@ -279,17 +295,15 @@ __device__ __forceinline__ float bias_at(const uint16_t* bias, int n, bool f16) 
   return f16 ? __half2float(__ushort_as_half(b)) : __uint_as_float(static_cast<uint32_t>(b) << 16);
 }
 
-// Scale, bias and round 32 accumulator columns of one row and store them.
-// cs / cb: this chunk's 32 column scales / bias values in shared memory.
+// Scale, bias and round 32 accumulator columns of one row into 16 packed
+// pairs (first column in the low half).  cs / cb: this chunk's 32 column
+// scales / bias values in shared memory.
 template <bool F16OUT>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32_t (&r)[32],
-                                               const float* cs, const float* cb, float sa,
-                                               bool col_scale, bool has_bias, uint16_t* crow,
-                                               int n0) {
-  const bool full = (n0 + 32 <= p.N);
+__device__ __forceinline__ void epilogue_values(const GemmParams& p, const uint32_t (&r)[32],
+                                                const float* cs, const float* cb, float sa,
+                                                bool col_scale, bool has_bias, uint32_t* o) {
   const uint64_t sa2 = pack_f32x2(sa, sa);
   const uint64_t sb2 = pack_f32x2(p.b_scale, p.b_scale);
-  uint32_t o[16];
 #pragma unroll
   for (int j = 0; j < 32; j += 4) {
     float4 sc = make_float4(0.f, 0.f, 0.f, 0.f), bi = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -309,6 +323,17 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
       o[j / 2 + h] = pack2(y0, y1, F16OUT);
     }
   }
+}
+
+// epilogue_values for 32 columns of one row, stored to C.
+template <bool F16OUT>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32_t (&r)[32],
+                                               const float* cs, const float* cb, float sa,
+                                               bool col_scale, bool has_bias, uint16_t* crow,
+                                               int n0) {
+  const bool full = (n0 + 32 <= p.N);
+  uint32_t o[16];
+  epilogue_values<F16OUT>(p, r, cs, cb, sa, col_scale, has_bias, o);
   if (full && p.vec_store) {
     uint4* dst = reinterpret_cast<uint4*>(crow + n0);
 #pragma unroll
@@ -392,7 +417,123 @@ __device__ void gemm_epilogue(const GemmParams& p, const GemmBars& bar, uint32_t
   }
 }
 
-template <bool PAIR, bool BKM, bool F16OUT>
+// Fused QKV quantize epilogue (p.qkv_S > 0).  A CTA's 128 rows are one
+// 128-token block of one batch and each half of the tile's 256 columns is one
+// head of Q, K or V, so the four warps of a half (one per TMEM lane quarter)
+// hold exactly one scale group of the per-block quantizer: 128 tokens x 128
+// head dims of one (batch, head).  Each thread keeps its row's 128 bf16
+// values (the bf16 C the plain epilogue would store, bit for bit), the four
+// warps combine their block amax through shared memory and a named barrier,
+// and every thread quantizes its row with the quantizer's own steps
+// (quant_common.cuh) and writes its 128 e4m3 bytes into the attention
+// kernel's (B * H, S, 128) layout; one thread writes the block's scale.
+template <bool PAIR>
+__device__ void gemm_epilogue_qkv(const GemmParams& p, const GemmBars& bar, uint32_t tmem,
+                                  float* colbuf, uint32_t* amax_slots, uint32_t rank) {
+  using C = GCfg<PAIR>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ew = warp - 2;
+  const int q = warp & 3;
+  const int half = ew / 4;
+  const bool col_scale = p.sb != nullptr, has_bias = p.bias != nullptr;
+  float* cs = colbuf + ew * 2 * kEpiCols;
+  float* cb = cs + kEpiCols;
+  const int H = p.qkv_H, S = p.qkv_S;
+  int it = 0;
+  for (int t = tile_unit<PAIR>(); t < p.tiles; t += tile_units<PAIR>(), ++it) {
+    const int buf = it & 1;
+    const TileCoord c = tile_coord(p, t);
+    const int b = c.m / p.qkv_per_b;
+    const int s0 = (c.m - b * p.qkv_per_b) * C::kTileM + static_cast<int>(rank) * kCtaRows;
+    const int cblk = c.n * 2 + half;  // 128-column block: which * H + head
+    const bool blk_ok = cblk < 3 * H && s0 < S;
+    const int ncol0 = c.n * kTileN + half * kEpiCols;
+    if (col_scale || has_bias) {
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < kEpiCols / 32; ++i) {
+        const int n = ncol0 + i * 32 + lane;
+        const bool in = n < p.N;
+        if (col_scale) cs[i * 32 + lane] = in ? __ldg(p.sb + (int64_t)n * p.sb_stride) : 0.f;
+        if (has_bias) cb[i * 32 + lane] = in ? bias_at(p.bias, n, false) : 0.f;
+      }
+      __syncwarp();
+    }
+    const int s = s0 + q * 32 + lane;  // this thread's token
+    const bool row_ok = blk_ok && s < S;
+    const int64_t m = (int64_t)b * S + s;
+    const float sa = p.sa ? (row_ok ? __ldg(p.sa + m * p.sa_stride) : 0.f) : p.a_scale;
+    if (!wait_bar<PAIR>(bar.acc_full + buf, (it >> 1) & 1, bar, p.status, kErrGemmAccFull))
+      return;
+    tc_fence_after();
+    const uint32_t taddr =
+        tmem + buf * kTileN + half * kEpiCols + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t y[kEpiCols / 2];  // the row's 128 bf16 values, packed pairs
+#pragma unroll
+    for (int pr = 0; pr < kEpiCols / 64; ++pr) {
+      uint32_t r0[32], r1[32];
+      if (p.n_kb > 0) {
+        tmem_ld32(taddr + pr * 64, r0);
+        tmem_ld32(taddr + pr * 64 + 32, r1);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r0[j] = r1[j] = 0u;
+      }
+      if (pr == kEpiCols / 64 - 1) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(mapa_shared(smem_u32(bar.acc_empty + buf), 0));
+          else
+            mbar_arrive(bar.acc_empty + buf);
+        }
+      }
+      epilogue_values<false>(p, r0, cs + pr * 64, cb + pr * 64, sa, col_scale, has_bias, y + pr * 32);
+      epilogue_values<false>(p, r1, cs + pr * 64 + 32, cb + pr * 64 + 32, sa, col_scale, has_bias,
+                             y + pr * 32 + 16);
+    }
+    // block amax: |bf16| bit patterns (NaN above +inf), valid rows only
+    uint32_t am = 0;
+    if (row_ok) {
+      uint32_t a2 = 0;
+#pragma unroll
+      for (int i = 0; i < kEpiCols / 2; ++i) a2 = __vmaxu2(a2, y[i] & 0x7FFF7FFFu);
+      am = max(a2 & 0xFFFFu, a2 >> 16);
+    }
+    am = __reduce_max_sync(0xffffffffu, am);
+    uint32_t* slots = amax_slots + (buf * 2 + half) * 4;
+    if (lane == 0) slots[q] = am;
+    named_bar_sync(1 + half, 128);
+    const uint32_t bm = max(max(slots[0], slots[1]), max(slots[2], slots[3]));
+    if (blk_ok) {
+      const float sc = quant::scale_from_amax_bits<false>(bm);
+      const float qm = __frcp_rn(sc);
+      const bool fast = isfinite(sc);
+      const int which = cblk / H, h = cblk - which * H;
+      if (row_ok) {
+        // (conditional picks, not a dynamic index into the parameter struct)
+        uint8_t* out8 = which == 0 ? p.qkv_out[0] : (which == 1 ? p.qkv_out[1] : p.qkv_out[2]);
+        uint4* dst = reinterpret_cast<uint4*>(out8 + ((int64_t)(b * H + h) * S + s) * 128);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const uint2 lo = quant::quant8_any<false>(
+              make_uint4(y[8 * v], y[8 * v + 1], y[8 * v + 2], y[8 * v + 3]), qm, fast);
+          const uint2 hi = quant::quant8_any<false>(
+              make_uint4(y[8 * v + 4], y[8 * v + 5], y[8 * v + 6], y[8 * v + 7]), qm, fast);
+          dst[v] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+      }
+      if (q == 0 && lane == 0) {
+        float* sd = which == 0 ? p.qkv_scales[0] : (which == 1 ? p.qkv_scales[1] : p.qkv_scales[2]);
+        sd[(int64_t)(b * H + h) * p.qkv_nblk + s0 / kCtaRows] = sc;
+      }
+    }
+  }
+}
+
+template <bool PAIR, bool BKM, bool F16OUT, bool QKV = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
@@ -444,7 +585,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     if (lane == 0 && rank == 0) gemm_mma<PAIR, BKM>(p, bar, smem_u32(smem), tmem);
   } else {
-    gemm_epilogue<PAIR, F16OUT>(p, bar, tmem, reinterpret_cast<float*>(smem + C::kOffCol), rank);
+    if constexpr (QKV)
+      gemm_epilogue_qkv<PAIR>(p, bar, tmem, reinterpret_cast<float*>(smem + C::kOffCol),
+                              reinterpret_cast<uint32_t*>(smem + C::kOffAmax), rank);
+    else
+      gemm_epilogue<PAIR, F16OUT>(p, bar, tmem, reinterpret_cast<float*>(smem + C::kOffCol), rank);
   }
   __syncwarp();
 
@@ -464,11 +609,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool PAIR, bool BKM, bool F16OUT>
+template <bool PAIR, bool BKM, bool F16OUT, bool QKV = false>
 cudaError_t launch_gemm_variant(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
                                 int units, cudaStream_t st) {
   using C = GCfg<PAIR>;
-  auto kern = fp8_gemm_kernel<PAIR, BKM, F16OUT>;
+  auto kern = fp8_gemm_kernel<PAIR, BKM, F16OUT, QKV>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -544,7 +689,13 @@ template <bool PAIR>
 cudaError_t launch_fp8_gemm_t(const CUtensorMap& a, const CUtensorMap& b, GemmParams p,
                               bool b_kmajor, bool out_f16, cudaStream_t st) {
   using C = GCfg<PAIR>;
-  p.tiles_m = (p.M + C::kTileM - 1) / C::kTileM;
+  if (p.qkv_S > 0) {
+    if (!b_kmajor || out_f16 || p.qkv_S <= 0 || p.M % p.qkv_S != 0) return cudaErrorInvalidValue;
+    p.qkv_per_b = (p.qkv_S + C::kTileM - 1) / C::kTileM;
+    p.tiles_m = (p.M / p.qkv_S) * p.qkv_per_b;
+  } else {
+    p.tiles_m = (p.M + C::kTileM - 1) / C::kTileM;
+  }
   p.tiles_n = (p.N + kTileN - 1) / kTileN;
   p.tiles = p.tiles_m * p.tiles_n;
   p.n_kb = (p.K + kBK - 1) / kBK;
@@ -553,6 +704,7 @@ cudaError_t launch_fp8_gemm_t(const CUtensorMap& a, const CUtensorMap& b, GemmPa
   if (p.group_m > p.tiles_m) p.group_m = p.tiles_m;
   const int slots = PAIR ? sm_count() / 2 : sm_count();
   const int units = p.tiles < slots ? p.tiles : slots;
+  if (p.qkv_S > 0) return launch_gemm_variant<PAIR, true, false, true>(a, b, p, units, st);
   if (b_kmajor)
     return out_f16 ? launch_gemm_variant<PAIR, true, true>(a, b, p, units, st)
                    : launch_gemm_variant<PAIR, true, false>(a, b, p, units, st);

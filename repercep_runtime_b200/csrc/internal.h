@@ -66,9 +66,20 @@ struct GemmParams {
   int64_t ldc;
   int vec_store;         // C and ldc allow 16-byte stores
   int* status;           // device status word (0 = ok)
+  // Fused QKV quantize (qkv_S > 0; B (N, K), bf16 rounding): the rows are
+  // M / qkv_S batches of qkv_S tokens and the N = 3 * qkv_H * 128 columns are
+  // Q, K, V of qkv_H heads.  Instead of writing C, every 128-token block of
+  // every (batch, head) of Q, K and V is quantized to e4m3, as the attention
+  // quantizer's per-block mode does on C: qkv_out[i] (B * H, S, 128) e4m3 and
+  // qkv_scales[i] (B * H, qkv_nblk) fp32.  qkv_per_b (row tiles per batch) is
+  // filled by launch_fp8_gemm.
+  int qkv_S, qkv_H, qkv_nblk, qkv_per_b;
+  uint8_t* qkv_out[3];
+  float* qkv_scales[3];
 };
 
 // b_kmajor: B is (N, K) with K contiguous; otherwise (K, N) with N contiguous.
+// A fused QKV quantize (p.qkv_S > 0) needs b_kmajor and a bf16 rounding.
 cudaError_t launch_fp8_gemm(const CUtensorMap& a, const CUtensorMap& b, GemmParams p,
                             bool b_kmajor, bool out_f16, cudaStream_t st);
 // Rows of the B box the selected kernel loads per K block (K-major B: the

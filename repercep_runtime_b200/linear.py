@@ -221,3 +221,88 @@ class Fp8Linear(torch.nn.Module):
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, e4m3"
+
+
+def gemm_qkv_quant(
+    x8: torch.Tensor,
+    w8: torch.Tensor,
+    sa: torch.Tensor | float,
+    sb: torch.Tensor | float,
+    heads: int,
+    seq_len: int,
+    bias: torch.Tensor | None = None,
+) -> list:
+    """The QKV projection with the attention quantizer fused into its epilogue.
+
+    ``x8`` (B*S, K) e4m3 activations, B batches of ``seq_len`` tokens;
+    ``w8`` (3*heads*128, K) e4m3, the stacked Q, K, V projection weights
+    (head-major inside each); ``sa`` / ``sb`` per-token / per-channel fp32
+    scales (or floats); ``bias`` (3*heads*128,) bf16 or None.  Returns
+    ``ops.Quantized`` q, k, v: (B, heads, S, 128) e4m3 with per-128-token-block
+    scales, ready for ``ops.attention_fp8_quantized``.  Bit for bit the
+    per-block ``ops.quantize_fp8`` of the bf16 ``gemm_ex`` output viewed as
+    (B, S, 3, heads, 128) (the reference quantizes right before its kernel,
+    kernels/triton_kernels/fp8_flash_attn_hopper.py:474-480); the bf16
+    projection output is never written.
+    """
+    from . import ops
+
+    if x8.dim() != 2 or w8.dim() != 2:
+        raise ValueError("x8 and w8 must be 2-D")
+    if x8.dtype != FP8 or w8.dtype != FP8:
+        raise ValueError("x8 and w8 must be float8_e4m3fn")
+    M, K = (int(s) for s in x8.shape)
+    N = 3 * heads * 128
+    if heads <= 0 or seq_len <= 0 or M % seq_len != 0:
+        raise ValueError(f"{M} rows are not whole batches of seq_len={seq_len}")
+    if tuple(w8.shape) != (N, K):
+        raise ValueError(f"w8 must be ({N}, {K}) for {heads} heads of 128, got {tuple(w8.shape)}")
+    B = M // seq_len
+    dev = x8.device
+
+    def scale_arg(s, n: int, name: str):  # type: ignore[no-untyped-def]
+        if isinstance(s, torch.Tensor):
+            if s.dtype != torch.float32 or s.device != dev:
+                raise ValueError(f"{name} must be fp32 on {dev}")
+            if s.numel() == 1:
+                return s, 0, 1.0
+            if s.numel() != n or s.dim() != 1:
+                raise ValueError(f"{name} must hold 1 or {n} scales")
+            return s, int(s.stride(0)), 1.0
+        return None, 0, float(s)
+
+    sa_t, sa_stride, a_scale = scale_arg(sa, M, "sa")
+    sb_t, sb_stride, b_scale = scale_arg(sb, N, "sb")
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or bias.numel() != N or bias.device != dev:
+            raise ValueError(f"bias must be ({N},) bf16 on {dev}")
+        bias = bias.contiguous()
+    nblk = (seq_len + ops.BLOCK - 1) // ops.BLOCK
+    outs = [torch.empty((B, heads, seq_len, 128), dtype=FP8, device=dev) for _ in range(3)]
+    scales = [torch.empty((B * heads, nblk), dtype=torch.float32, device=dev) for _ in range(3)]
+    a = _pitched(x8, 16)
+    w = _pitched(w8, 16)
+    lib = _lib.load()
+    rc = lib.rp_fp8_gemm_qkv_quant(
+        a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0),
+        sa_t.data_ptr() if sa_t is not None else None, sa_stride, a_scale,
+        sb_t.data_ptr() if sb_t is not None else None, sb_stride, b_scale,
+        bias.data_ptr() if bias is not None else None, B, seq_len, heads, K,
+        outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(),
+        scales[0].data_ptr(), scales[1].data_ptr(), scales[2].data_ptr(), _stream(outs[0]),
+    )  # fmt: skip
+    _lib.check("rp_fp8_gemm_qkv_quant", rc)
+    return [ops.Quantized(o, s, ops.SCALE_PER_BLOCK128, 128) for o, s in zip(outs, scales)]
+
+
+def qkv_projection_fp8(
+    x: torch.Tensor, w8: torch.Tensor, ws: torch.Tensor, heads: int, bias: torch.Tensor | None = None
+) -> list:
+    """bf16 hidden states x (B, S, hidden) -> attention-ready e4m3 q, k, v:
+    per-token activation quantize, then the QKV GEMM with the per-block
+    quantizer in its epilogue (``gemm_qkv_quant``)."""
+    if x.dim() != 3:
+        raise ValueError("x must be (B, S, hidden)")
+    B, S, K = (int(s) for s in x.shape)
+    x8, xs = quantize_rows(x.reshape(B * S, K))
+    return gemm_qkv_quant(x8, w8, xs, ws, heads, S, bias)
