@@ -30,6 +30,8 @@
  *                             (bound by fp8_gemm, kernels/hip/fp8_attn/binding.cpp:24-61)
  *   rp_fp8_gemm_ex, rp_quant_fp8_rows <- (no reference kernel: FP8 DiT linears are the
  *                             reference's planned use of that GEMM, docs/OPTIMIZATION.md:161-162)
+ *   rp_quant_fp8_e4m3_bh_phase <- _per_bh_scale + _quantize split at the amax, for a sequence
+ *                             split across devices (the reference has no context parallelism)
  *   rp_fp8_gemm_qkv_quant  <- the QKV projection followed by the eager quantize of Q, K, V,
  *                             fp8_flash_attn_hopper.py:474-480 (per-128-token-block mode)
  */
@@ -121,6 +123,31 @@ int rp_quant_fp8_e4m3_ex(int num_tensors, const void* const* x, const int64_t* s
                          int H, int S, int D, int in_dtype, int scale_mode, void* const* out,
                          int out_row_bytes, float* const* scales, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* The two phases of the per-(b,h) quantizer, for a sequence split across
+ * devices (context parallelism): the reference's per-(b,h) scale
+ * (_per_bh_scale, fp8_flash_attn_hopper.py:374-385) is an amax over the whole
+ * sequence, so each device computes the partial amax of its own tokens, the
+ * devices combine them with an element-wise max, and each quantizes its
+ * tokens with the common scale.
+ *   RP_QUANT_PHASE_AMAX   writes the |x| max (bit patterns; NaN above +inf) of
+ *                         each 128-token chunk of each (tensor, b, h) to
+ *                         partials[(i * B*H + bh) * npart + chunk] for chunk <
+ *                         ceil(S/128); the other slots are left as they are
+ *                         (zero them: 0 is the max's identity);
+ *   RP_QUANT_PHASE_APPLY  takes each (tensor, b, h)'s scale from the max of
+ *                         its npart slots and quantizes x into out / scales
+ *                         exactly as rp_quant_fp8_e4m3_ex (RP_SCALE_PER_BH).
+ * Combining the partial arrays of all devices with an element-wise integer
+ * max (e.g. an all-reduce MAX on int32) between the phases gives every device
+ * the scales of the whole sequence, and bytes identical to quantizing the
+ * whole sequence on one device.  npart >= ceil(S/128).  The amax phase reads
+ * no out / scales (they may be NULL). */
+enum { RP_QUANT_PHASE_AMAX = 1, RP_QUANT_PHASE_APPLY = 2 };
+int rp_quant_fp8_e4m3_bh_phase(int phase, int num_tensors, const void* const* x,
+                               const int64_t* strides, int B, int H, int S, int D, int in_dtype,
+                               uint32_t* partials, int npart, void* const* out, int out_row_bytes,
+                               float* const* scales, void* stream);
 
 /* Allocation-free variant of rp_quant_fp8_e4m3 for RP_SCALE_PER_BH (no
  * counterpart in the reference, which always allocates through PyTorch).

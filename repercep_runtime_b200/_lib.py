@@ -23,6 +23,8 @@ RP_DTYPE_BF16 = 0
 RP_DTYPE_F16 = 1
 RP_B_KN = 0
 RP_B_NK = 1
+RP_QUANT_PHASE_AMAX = 1
+RP_QUANT_PHASE_APPLY = 2
 
 STATUS_NAMES = {
     -1: "RP_ERR_INVALID",
@@ -158,6 +160,26 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rp_quant_fp8_rows": (
         _c_int,
         [_c_void_p, ctypes.c_int64, _c_int, _c_int, _c_int, _c_void_p, ctypes.c_int64, _c_void_p, _c_void_p],
+    ),
+    "rp_quant_fp8_e4m3_bh_phase": (
+        _c_int,
+        [
+            _c_int,
+            _c_int,
+            _c_void_p,
+            _c_void_p,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_int,
+            _c_void_p,
+            _c_int,
+            _c_void_p,
+            _c_int,
+            _c_void_p,
+            _c_void_p,
+        ],
     ),
     "rp_fp8_gemm_qkv_quant": (
         _c_int,

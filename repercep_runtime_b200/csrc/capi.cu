@@ -241,10 +241,12 @@ int rp_quant_fp8_e4m3(int num_tensors, const void* const* x, const int64_t* stri
                               D, scales, workspace, workspace_bytes, stream);
 }
 
-int rp_quant_fp8_e4m3_ex(int num_tensors, const void* const* x, const int64_t* strides, int B,
-                         int H, int S, int D, int in_dtype, int scale_mode, void* const* out,
-                         int out_row_bytes, float* const* scales, void* workspace,
-                         size_t workspace_bytes, void* stream) {
+namespace {
+
+// Checks shared by the quantizer entry points; fills `a` (without partials).
+int quant_args(int num_tensors, const void* const* x, const int64_t* strides, int B, int H, int S,
+               int D, int in_dtype, void* const* out, int out_row_bytes, float* const* scales,
+               rp::QuantArgs* a, bool need_out = true) {
   if (in_dtype != RP_DTYPE_BF16 && in_dtype != RP_DTYPE_F16)
     return fail(RP_ERR_UNSUPPORTED, "input dtype %d is neither bf16 nor fp16", in_dtype);
   if (out_row_bytes < D || out_row_bytes % 16)
@@ -252,46 +254,85 @@ int rp_quant_fp8_e4m3_ex(int num_tensors, const void* const* x, const int64_t* s
                 out_row_bytes, D);
   if (num_tensors < 1 || num_tensors > rp::kMaxQuantJobs)
     return fail(RP_ERR_INVALID, "num_tensors must be 1..3 (got %d)", num_tensors);
-  if (!x || !strides || !out || !scales) return fail(RP_ERR_INVALID, "null argument array");
+  if (!x || !strides || (need_out && (!out || !scales)))
+    return fail(RP_ERR_INVALID, "null argument array");
   if (B <= 0 || H <= 0 || S <= 0) return fail(RP_ERR_INVALID, "B, H, S must be positive");
   if (D != 32 && D != 64 && D != 128 && D != 256)
     return fail(RP_ERR_UNSUPPORTED, "head_dim %d not in {32,64,128,256}", D);
   if ((int64_t)B * H > 65535) return fail(RP_ERR_UNSUPPORTED, "B*H > 65535");
+  *a = rp::QuantArgs{};
+  a->B = B;
+  a->H = H;
+  a->S = S;
+  a->D = D;
+  a->in_f16 = (in_dtype == RP_DTYPE_F16) ? 1 : 0;
+  a->out_ld = out_row_bytes;
+  a->nblk = ceil_div(S, rp::kQuantRows);
+  a->npart = a->nblk;
+  for (int i = 0; i < num_tensors; ++i) {
+    const int64_t* st = strides + 4 * i;
+    if (!x[i] || (need_out && (!out[i] || !scales[i])))
+      return fail(RP_ERR_INVALID, "tensor %d: null pointer", i);
+    if (st[3] != 1) return fail(RP_ERR_UNSUPPORTED, "tensor %d: head dim must be unit-stride", i);
+    if (!aligned16(x[i]) || (st[0] % 8) || (st[1] % 8) || (st[2] % 8))
+      return fail(RP_ERR_ALIGN, "tensor %d: base and strides must be 16-byte multiples", i);
+    if (need_out && !aligned16(out[i]))
+      return fail(RP_ERR_ALIGN, "tensor %d: output must be 16-byte aligned", i);
+    a->job[i].x = static_cast<const uint16_t*>(x[i]);
+    a->job[i].sB = st[0];
+    a->job[i].sH = st[1];
+    a->job[i].sS = st[2];
+    a->job[i].out = need_out ? static_cast<uint8_t*>(out[i]) : nullptr;
+    a->job[i].scales = need_out ? scales[i] : nullptr;
+  }
+  return RP_OK;
+}
+
+}  // namespace
+
+int rp_quant_fp8_e4m3_ex(int num_tensors, const void* const* x, const int64_t* strides, int B,
+                         int H, int S, int D, int in_dtype, int scale_mode, void* const* out,
+                         int out_row_bytes, float* const* scales, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  rp::QuantArgs a;
+  int rc = quant_args(num_tensors, x, strides, B, H, S, D, in_dtype, out, out_row_bytes, scales, &a);
+  if (rc != RP_OK) return rc;
   size_t need = 0;
-  int rc = rp_quant_workspace_bytes(num_tensors, B, H, S, D, scale_mode, &need);
+  rc = rp_quant_workspace_bytes(num_tensors, B, H, S, D, scale_mode, &need);
   if (rc != RP_OK) return rc;
   if (need > 0 && (!workspace || workspace_bytes < need))
     return fail(RP_ERR_WORKSPACE, "workspace of %zu bytes required", need);
   int* status = nullptr;
   rc = device_ready(&status);
   if (rc != RP_OK) return rc;
-
-  rp::QuantArgs a{};
-  a.B = B;
-  a.H = H;
-  a.S = S;
-  a.D = D;
-  a.in_f16 = (in_dtype == RP_DTYPE_F16) ? 1 : 0;
-  a.out_ld = out_row_bytes;
-  a.nblk = ceil_div(S, rp::kQuantRows);
   a.partial = static_cast<uint32_t*>(workspace);
-  for (int i = 0; i < num_tensors; ++i) {
-    const int64_t* st = strides + 4 * i;
-    if (!x[i] || !out[i] || !scales[i]) return fail(RP_ERR_INVALID, "tensor %d: null pointer", i);
-    if (st[3] != 1) return fail(RP_ERR_UNSUPPORTED, "tensor %d: head dim must be unit-stride", i);
-    if (!aligned16(x[i]) || (st[0] % 8) || (st[1] % 8) || (st[2] % 8))
-      return fail(RP_ERR_ALIGN, "tensor %d: base and strides must be 16-byte multiples", i);
-    if (!aligned16(out[i])) return fail(RP_ERR_ALIGN, "tensor %d: output must be 16-byte aligned", i);
-    a.job[i].x = static_cast<const uint16_t*>(x[i]);
-    a.job[i].sB = st[0];
-    a.job[i].sH = st[1];
-    a.job[i].sS = st[2];
-    a.job[i].out = static_cast<uint8_t*>(out[i]);
-    a.job[i].scales = scales[i];
-  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = (scale_mode == RP_SCALE_PER_BLOCK128) ? rp::launch_quant_block(a, num_tensors, s)
                                                         : rp::launch_quant_bh(a, num_tensors, s);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  return RP_OK;
+}
+
+int rp_quant_fp8_e4m3_bh_phase(int phase, int num_tensors, const void* const* x,
+                               const int64_t* strides, int B, int H, int S, int D, int in_dtype,
+                               uint32_t* partials, int npart, void* const* out, int out_row_bytes,
+                               float* const* scales, void* stream) {
+  if (phase != RP_QUANT_PHASE_AMAX && phase != RP_QUANT_PHASE_APPLY)
+    return fail(RP_ERR_INVALID, "unknown phase %d", phase);
+  rp::QuantArgs a;
+  int rc = quant_args(num_tensors, x, strides, B, H, S, D, in_dtype, out, out_row_bytes, scales, &a,
+                      phase == RP_QUANT_PHASE_APPLY);
+  if (rc != RP_OK) return rc;
+  if (!partials) return fail(RP_ERR_INVALID, "partials is null");
+  if (npart < a.nblk)
+    return fail(RP_ERR_INVALID, "npart %d is below ceil(S/128) = %d", npart, a.nblk);
+  int* status = nullptr;
+  rc = device_ready(&status);
+  if (rc != RP_OK) return rc;
+  a.partial = partials;
+  a.npart = npart;
+  cudaError_t e = rp::launch_quant_bh(a, num_tensors, static_cast<cudaStream_t>(stream),
+                                      phase == RP_QUANT_PHASE_AMAX ? 1 : 2);
   if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
   return RP_OK;
 }

@@ -29,12 +29,15 @@ struct QuantArgs {
   int in_f16;          // 0: bf16 input, 1: fp16 input
   int out_ld;          // output row pitch in bytes (>= D, multiple of 16; padding zeroed)
   int nblk;            // ceil(S / 128)
-  uint32_t* partial;   // per-(b,h) mode: (njobs, B*H, nblk) partial amax bits
+  uint32_t* partial;   // per-(b,h) mode: (njobs, B*H, npart) partial amax bits
+  int npart;           // per-(b,h) mode: partial slots per (job, b*h), >= nblk
 };
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_quant_block(const QuantArgs& a, int njobs, cudaStream_t st);
-cudaError_t launch_quant_bh(const QuantArgs& a, int njobs, cudaStream_t st);
+// phases: 1 = partial amax of each 128-token chunk, 2 = scale from the npart
+// partials of each (job, b*h) and quantize, 3 = both.
+cudaError_t launch_quant_bh(const QuantArgs& a, int njobs, cudaStream_t st, int phases = 3);
 
 // Row-wise quantizer of a linear operand: one scale per row of (rows, cols).
 struct QuantRowsArgs {

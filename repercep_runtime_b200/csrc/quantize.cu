@@ -130,19 +130,19 @@ __global__ void __launch_bounds__(kQuantThreads) amax_chunk_kernel(const QuantAr
   }
   m = block_max(m, red);
   if (threadIdx.x == 0)
-    a.partial[((int64_t)blockIdx.z * gridDim.y + bh) * a.nblk + blk] = m;
+    a.partial[((int64_t)blockIdx.z * gridDim.y + bh) * a.npart + blk] = m;
 }
 
-// Per-(b,h) pass 2: reduce the partials of this (b,h), quantize one chunk.
+// Per-(b,h) pass 2: reduce the npart partials of this (b,h), quantize one chunk.
 template <int D, bool F16>
 __global__ void __launch_bounds__(kQuantThreads) quant_bh_kernel(const QuantArgs a) {
   __shared__ uint32_t red[kQuantThreads / 32];
   const QuantJob& j = a.job[blockIdx.z];
   const int blk = blockIdx.x, bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
-  const uint32_t* part = a.partial + ((int64_t)blockIdx.z * gridDim.y + bh) * a.nblk;
+  const uint32_t* part = a.partial + ((int64_t)blockIdx.z * gridDim.y + bh) * a.npart;
   uint32_t m = 0;
-  for (int i = threadIdx.x; i < a.nblk; i += kQuantThreads) m = max(m, part[i]);
+  for (int i = threadIdx.x; i < a.npart; i += kQuantThreads) m = max(m, part[i]);
   m = block_max(m, red);
   const float sc = scale_from_amax_bits<F16>(m);
   if (blk == 0 && threadIdx.x == 0) j.scales[bh] = sc;
@@ -266,12 +266,16 @@ cudaError_t launch_quant_block(const QuantArgs& a, int njobs, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_quant_bh(const QuantArgs& a, int njobs, cudaStream_t st) {
+cudaError_t launch_quant_bh(const QuantArgs& a, int njobs, cudaStream_t st, int phases) {
   const dim3 grid(a.nblk, a.B * a.H, njobs);
-  RP_DISPATCH_D(amax_chunk_kernel)
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  RP_DISPATCH_D(quant_bh_kernel)
+  if (phases & 1) {
+    RP_DISPATCH_D(amax_chunk_kernel)
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (phases & 2) {
+    RP_DISPATCH_D(quant_bh_kernel)
+  }
   return cudaGetLastError();
 }
 

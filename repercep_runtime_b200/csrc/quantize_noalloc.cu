@@ -100,6 +100,7 @@ extern "C" int rp_quant_fp8_e4m3_noalloc(int num_tensors, const void* const* x,
   a.in_f16 = 0;
   a.out_ld = D;
   a.nblk = nblk;
+  a.npart = nblk;
   for (int i = 0; i < num_tensors; ++i) {
     const int64_t* st = strides + 4 * i;
     if (!x[i] || !out[i] || !scales[i]) return set_last_error(RP_ERR_INVALID, "tensor %d: null pointer", i);

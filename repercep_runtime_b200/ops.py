@@ -74,6 +74,89 @@ class Quantized:
 _DTYPES = {torch.bfloat16: _lib.RP_DTYPE_BF16, torch.float16: _lib.RP_DTYPE_F16}
 
 
+def _bh_phase(phase: int, xs, partials: torch.Tensor, layout: str, row_bytes: int | None):  # type: ignore[no-untyped-def]
+    lib = _lib.load()
+    B, H, S, D = bhsd_shape(xs[0], layout)
+    row = D if row_bytes is None else int(row_bytes)
+    dtype = xs[0].dtype
+    if dtype not in _DTYPES:
+        raise ValueError(f"inputs must be bf16 or fp16, got {dtype}")
+    nblk = (S + BLOCK - 1) // BLOCK
+    if partials.dtype != torch.int32 or partials.dim() != 3 or tuple(partials.shape[:2]) != (len(xs), B * H):
+        raise ValueError(f"partials must be int32 ({len(xs)}, {B * H}, npart)")
+    npart = int(partials.shape[2])
+    if npart < nblk or not partials.is_contiguous():
+        raise ValueError(f"partials need >= ceil(S/128) = {nblk} contiguous slots per row")
+    outs, scales, strides = [], [], []
+    for i, x in enumerate(xs):
+        _require_cuda(x, f"x[{i}]", dtype)
+        if bhsd_shape(x, layout) != (B, H, S, D):
+            raise ValueError("all tensors must share one shape")
+        if phase == _lib.RP_QUANT_PHASE_APPLY:
+            outs.append(torch.empty((B, H, S, row), dtype=FP8, device=x.device))
+            scales.append(torch.empty((B * H,), dtype=torch.float32, device=x.device))
+        strides.extend(bhsd_strides(x, layout))
+    apply = phase == _lib.RP_QUANT_PHASE_APPLY  # the amax phase takes no outputs
+    rc = lib.rp_quant_fp8_e4m3_bh_phase(
+        phase, len(xs), _lib.ptr_array(x.data_ptr() for x in xs), _lib.i64_array(strides),
+        B, H, S, D, _DTYPES[dtype], partials.data_ptr(), npart,
+        _lib.ptr_array(o.data_ptr() for o in outs) if apply else None, row,
+        _lib.ptr_array(s.data_ptr() for s in scales) if apply else None, _stream(xs[0]),
+    )  # fmt: skip
+    _lib.check("rp_quant_fp8_e4m3_bh_phase", rc)
+    return [Quantized(o, s, SCALE_PER_BH, D) for o, s in zip(outs, scales)]
+
+
+def quantize_fp8_bh_partials(xs, npart: int | None = None, layout: str = "bhsd") -> torch.Tensor:  # type: ignore[no-untyped-def]
+    """Phase 1 of the per-(b,h) quantizer for 1-3 tensors of one shape: the
+    |x| max (bit patterns) of every 128-token chunk, as an int32 (n, B*H,
+    npart) array with the slots past ceil(S/128) zero."""
+    if not 1 <= len(xs) <= 3:
+        raise ValueError("takes 1 to 3 tensors")
+    B, H, S, _ = bhsd_shape(xs[0], layout)
+    nblk = (S + BLOCK - 1) // BLOCK
+    partials = torch.zeros((len(xs), B * H, nblk if npart is None else int(npart)), dtype=torch.int32,
+                           device=xs[0].device)
+    _bh_phase(_lib.RP_QUANT_PHASE_AMAX, xs, partials, layout, None)
+    return partials
+
+
+def quantize_fp8_bh_apply(xs, partials: torch.Tensor, layout: str = "bhsd",  # type: ignore[no-untyped-def]
+                          row_bytes: int | None = None) -> list[Quantized]:
+    """Phase 2: per-(b,h) scales from the max of each row of ``partials``
+    (this tensor's chunks, or every rank's after an all-reduce MAX), then the
+    quantize -- ``quantize_fp8``'s per-(b,h) bytes and scales."""
+    return _bh_phase(_lib.RP_QUANT_PHASE_APPLY, xs, partials, layout, row_bytes)
+
+
+def quantize_fp8_bh_phased(
+    xs: list[torch.Tensor] | tuple[torch.Tensor, ...],
+    combine,  # type: ignore[no-untyped-def]
+    npart: int | None = None,
+    layout: str = "bhsd",
+    row_bytes: int | None = None,
+) -> list[Quantized]:
+    """Per-(b,h) quantize with ``combine(partials)`` between its two phases
+    (``rp_quant_fp8_e4m3_bh_phase``): ``combine`` may fold other devices'
+    partial maxima into the int32 array in place (an all-reduce MAX over the
+    ranks a sequence is split across), so the scales are those of the whole
+    sequence.  With a no-op ``combine`` this is ``quantize_fp8`` per-(b,h)."""
+    partials = quantize_fp8_bh_partials(xs, npart, layout)
+    combine(partials)
+    return quantize_fp8_bh_apply(xs, partials, layout, row_bytes)
+
+
+def per_block_view(q: Quantized) -> Quantized:
+    """A per-(b,h) ``Quantized`` with its scale repeated for every 128-token
+    block: the per-block kernels then compute exactly what the per-(b,h) ones
+    do (every block of a (b,h) reads the same scale)."""
+    if q.scale_mode == SCALE_PER_BLOCK128:
+        return q
+    S = int(q.data.shape[2])
+    nblk = (S + BLOCK - 1) // BLOCK
+    return Quantized(q.data, q.scales.reshape(-1, 1).expand(-1, nblk).contiguous(), SCALE_PER_BLOCK128, q.d)
+
+
 def attention_row_bytes(head_dim: int) -> int:
     """e4m3 row width the attention kernel reads for ``head_dim``."""
     return 128 if head_dim <= 128 else head_dim

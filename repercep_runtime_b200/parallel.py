@@ -18,6 +18,11 @@ src/repercep/attention/diffusers_backend.py:199-212):
   layout and the result is bit-identical to the single-GPU one.  Each rank
   owns complete query rows, so no partial outputs are exchanged.  Remote K/V
   always lands in this GPU's memory before any kernel reads it.
+  The reference's own per-(b,h) scale mode spans the whole sequence: each
+  rank computes the partial amax of its 128-token chunks, one all-reduce MAX
+  of those (B*H x chunks integers) gives every rank the whole sequence's
+  amax, and each rank quantizes its slice with the common scales -- again
+  bit-identical to one GPU.
 
 The collective is injected (``all_gather``), so the bookkeeping is testable
 with gloo ranks on CPU and an oracle in place of the kernel.
@@ -94,6 +99,17 @@ AllGather = Callable[["object", "object"], None]  # (output, input) -> None
 CP_CHUNKS = 2
 
 
+def nccl_all_reduce_max(group=None):  # type: ignore[no-untyped-def]
+    """In-place element-wise max over the ranks of ``group`` (the combine
+    step of the per-(b,h) scale under context parallelism)."""
+    import torch.distributed as dist
+
+    def reduce(t):  # type: ignore[no-untyped-def]
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+
+    return reduce
+
+
 def nccl_all_gather(group=None, high_priority: bool = True) -> AllGather:  # type: ignore[no-untyped-def]
     """``torch.distributed.all_gather_into_tensor`` bound to ``group``.
 
@@ -124,7 +140,9 @@ class ContextParallelAttention:
 
     ``__call__(q, k, v)`` takes this rank's (B, H, rows, D) bf16 shard (the
     rows of ``seq_shard(seq_len, rank, world)``) and returns the bf16 output
-    rows for it.
+    rows for it.  ``scale_mode``: per-128-token-block scales (default, no
+    collective before the gather) or the reference's per-(b,h) scales (one
+    all-reduce MAX of partial amaxes through ``all_reduce_max`` first).
     """
 
     def __init__(
@@ -135,11 +153,34 @@ class ContextParallelAttention:
         all_gather: AllGather | None = None,
         p_mode: int = 0,
         scale: float | None = None,
+        scale_mode: int = 1,
+        all_reduce_max=None,  # type: ignore[no-untyped-def]
     ) -> None:
+        if scale_mode not in (0, 1):
+            raise ValueError(f"unknown scale_mode {scale_mode}")
         self.shard = seq_shard(seq_len, rank, world)
         self.all_gather = all_gather
         self.p_mode = p_mode
         self.scale = scale
+        self.scale_mode = scale_mode
+        self.all_reduce_max = all_reduce_max
+        if scale_mode == 0 and world > 1 and all_reduce_max is None:
+            raise ValueError("per-(b,h) scales over several ranks need all_reduce_max")
+
+    def quantize(self, q, k, v):  # type: ignore[no-untyped-def]
+        """This rank's shards to e4m3 in the configured scale mode; per-(b,h)
+        scales are those of the whole sequence (partials combined across ranks)."""
+        from repercep_runtime_b200 import ops
+
+        if self.scale_mode == 1:
+            return ops.quantize_fp8((q, k, v), scale_mode=ops.SCALE_PER_BLOCK128)
+
+        def combine(partials):  # type: ignore[no-untyped-def]
+            if self.shard.world > 1:
+                self.all_reduce_max(partials)
+
+        # every rank's partial array has the same shape: chunk_rows/128 slots
+        return ops.quantize_fp8_bh_phased((q, k, v), combine, npart=self.shard.chunk_rows // BLOCK)
 
     def gather_kv(self, k8, v8, ks, vs):  # type: ignore[no-untyped-def]
         """All-gather this rank's e4m3 K/V (BH, rows, D) and per-block scales;
@@ -207,7 +248,7 @@ class ContextParallelAttention:
         if q.dtype != torch.bfloat16:
             raise ValueError("context-parallel attention takes bf16 shards")
         if sh.world == 1:
-            return fp8_attention_host(q, k, v, scale=self.scale, scale_mode=ops.SCALE_PER_BLOCK128,
+            return fp8_attention_host(q, k, v, scale=self.scale, scale_mode=self.scale_mode,
                                       p_mode=self.p_mode)
         bh = B * H
         plan = plan_chunks(bh, sh.chunk_rows)
@@ -269,10 +310,13 @@ class ContextParallelAttention:
         sh = self.shard
         if q.shape[2] != sh.rows or k.shape != q.shape or v.shape != q.shape:
             raise ValueError(f"expected (B, H, {sh.rows}, D) shards for rank {sh.rank}")
-        qq, kq, vq = ops.quantize_fp8((q, k, v), scale_mode=ops.SCALE_PER_BLOCK128)
+        qq, kq, vq = self.quantize(q, k, v)
         if sh.world == 1:
             return ops.attention_fp8_quantized(qq, kq, vq, scale=self.scale, p_mode=self.p_mode, out=out)
-        return self.attend_quantized(qq, kq, vq, out=out, chunks=chunks)
+        # the chunked kernel reads per-block scales; a per-(b,h) scale repeated
+        # over the blocks gives the per-(b,h) arithmetic exactly
+        return self.attend_quantized(ops.per_block_view(qq), ops.per_block_view(kq),
+                                     ops.per_block_view(vq), out=out, chunks=chunks)
 
     def attend_quantized(self, qq, kq, vq, out=None, chunks: int | None = None):  # type: ignore[no-untyped-def]
         """Gather K/V and attend, for quantized (per-128-block) shards.
@@ -323,6 +367,7 @@ __all__ = [
     "ContextParallelAttention",
     "SeqShard",
     "nccl_all_gather",
+    "nccl_all_reduce_max",
     "seq_shard",
     "shard_bh",
 ]

@@ -3,8 +3,10 @@
 With P ranks emulated on one GPU: each rank's e4m3 K/V chunk and scales are
 stacked as the all-gather would deliver them, and the chunked kernel runs each
 rank's queries against them.  Because shards are whole 128-token blocks, the
-result must equal the single-GPU per-block result bit for bit.  With two or
-more GPUs, the same check runs over NCCL with one process per GPU.
+result must equal the single-GPU per-block result bit for bit.  The
+reference's per-(b,h) scale mode is checked the same way (partial maxima
+combined across the emulated ranks first).  With two or more GPUs, both
+checks run over NCCL with one process per GPU.
 """
 
 from __future__ import annotations
@@ -58,6 +60,63 @@ def test_chunked_kernel_equals_single_gpu(S, world):
         assert torch.equal(out, ref[:, :, sh.start : sh.start + sh.rows]), f"rank {r}"
 
 
+@pytest.mark.parametrize("S,npart_extra", [(1000, 0), (333, 3), (4096, 1)])
+def test_phased_per_bh_quantize_equals_one_shot(S, npart_extra):
+    """The two phases with nothing combined in between (and spare zero
+    slots) give quantize_fp8's per-(b,h) bytes and scales."""
+    from repercep_runtime_b200 import ops
+
+    xs = [gen_bf16((2, 3, S, 128), "n1_outlier", 90 + i).cuda() for i in range(3)]
+    ref = ops.quantize_fp8(xs, scale_mode=ops.SCALE_PER_BH)
+    got = ops.quantize_fp8_bh_phased(xs, lambda part: None, npart=-(-S // 128) + npart_extra)
+    torch.cuda.synchronize()
+    for r, g in zip(ref, got):
+        assert torch.equal(r.data.view(torch.uint8), g.data.view(torch.uint8))
+        assert torch.equal(r.scales, g.scales)
+
+
+@pytest.mark.parametrize("S,world", [(1000, 3), (75600 // 16, 4), (300, 2)])
+def test_per_bh_context_parallel_emulated(S, world):
+    """The reference's per-(b,h) scales under context parallelism, P ranks
+    emulated on one GPU: every rank's partial maxima (chunk_rows/128 slots),
+    an element-wise max over the ranks (the all-reduce), each rank's slice
+    quantized with the common scales and attended against the stacked K/V.
+    Bytes, scales and outputs equal the single-GPU per-(b,h) ones."""
+    from repercep_runtime_b200 import ops
+    from repercep_runtime_b200.parallel import seq_shard
+
+    B, H, D = 1, 4, 128
+    q, k, v = (gen_bf16((B, H, S, D), "n1_outlier", 100 + i).cuda() for i in range(3))
+    full = ops.quantize_fp8((q, k, v), scale_mode=ops.SCALE_PER_BH)
+    ref = ops.attention_fp8_quantized(*full)
+    shards = [seq_shard(S, r, world) for r in range(world)]
+    ch = shards[0].chunk_rows
+    local = [[t[:, :, sh.start : sh.start + sh.rows] for t in (q, k, v)] for sh in shards]
+    parts = [ops.quantize_fp8_bh_partials(loc, npart=ch // 128) for loc in local]
+    combined = torch.stack(parts).amax(dim=0)
+    quant = [ops.quantize_fp8_bh_apply(loc, combined.clone()) for loc in local]
+    for r, sh in enumerate(shards):
+        for fq, lq in zip(full, quant[r]):
+            assert torch.equal(lq.scales, fq.scales), f"rank {r} scales"
+            assert torch.equal(lq.data.view(torch.uint8),
+                               fq.data.view(torch.uint8)[:, :, sh.start : sh.start + sh.rows]), f"rank {r}"
+    k_all = torch.zeros((world, B * H, ch, D), dtype=torch.uint8, device="cuda")
+    v_all = torch.zeros_like(k_all)
+    ks_all = torch.zeros((world, B * H, ch // 128), dtype=torch.float32, device="cuda")
+    vs_all = torch.zeros_like(ks_all)
+    for r, sh in enumerate(shards):
+        _, kq, vq = (ops.per_block_view(x) for x in quant[r])
+        k_all[r, :, : sh.rows] = kq.data.view(torch.uint8).reshape(B * H, sh.rows, D)
+        v_all[r, :, : sh.rows] = vq.data.view(torch.uint8).reshape(B * H, sh.rows, D)
+        ks_all[r, :, : kq.scales.shape[1]] = kq.scales
+        vs_all[r, :, : vq.scales.shape[1]] = vq.scales
+    for r, sh in enumerate(shards):
+        out = ops.attention_fp8_chunked(ops.per_block_view(quant[r][0]), k_all.view(ops.FP8),
+                                        v_all.view(ops.FP8), ks_all, vs_all, last_rows=shards[0].last_rows)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref[:, :, sh.start : sh.start + sh.rows]), f"rank {r}"
+
+
 def test_context_parallel_world_one_is_the_plain_call():
     from repercep_runtime_b200.parallel import ContextParallelAttention
 
@@ -93,6 +152,18 @@ def _nccl_worker(rank: int, world: int, port: int, S: int) -> None:
         host = [t[:, :, sl].contiguous().cpu().pin_memory() for t in (q, k, v)]
         out_h = cp(*host)
         assert out_h.device.type == "cpu" and torch.equal(out_h, ref.cpu()), f"rank {rank} (host)"
+        # the reference's per-(b,h) scales: partial maxima all-reduced first
+        from repercep_runtime_b200 import ops
+        from repercep_runtime_b200.parallel import nccl_all_reduce_max
+
+        cpb = ContextParallelAttention(S, rank, world, all_gather=nccl_all_gather(), scale_mode=0,
+                                       all_reduce_max=nccl_all_reduce_max())
+        out_b = cpb(q[:, :, sl].contiguous(), k[:, :, sl].contiguous(), v[:, :, sl].contiguous())
+        ref_b = ops.fp8_attention(q, k, v, scale_mode=ops.SCALE_PER_BH)[:, :, sl]
+        torch.cuda.synchronize()
+        assert torch.equal(out_b, ref_b), f"rank {rank} (per-(b,h))"
+        out_bh = cpb(*host)
+        assert torch.equal(out_bh, ref_b.cpu()), f"rank {rank} (per-(b,h), host)"
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -143,3 +143,47 @@ def _async_chunk_worker(rank: int, world: int, port: int, S: int) -> None:
 @pytest.mark.parametrize("S,world", [(300, 2), (700, 3)])
 def test_chunked_async_gathers_match_one_gather(S, world):
     mp.spawn(_async_chunk_worker, args=(world, _free_port(), S), nprocs=world, join=True)
+
+
+def _bh_scale_worker(rank: int, world: int, port: int, S: int) -> None:
+    """Per-(b,h) scales under context parallelism on gloo ranks, the oracle in
+    place of the two quantizer phases: each rank's chunk maxima in
+    chunk_rows/128 slots, combined by ``nccl_all_reduce_max`` (bound to the
+    gloo group), give the whole sequence's scales and bytes."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from helpers import bits, gen_bf16
+        from oracle import quantize as oq
+        from repercep_runtime_b200.parallel import nccl_all_reduce_max
+
+        B, H, D = 2, 3, 64
+        full = gen_bf16((B, H, S, D), "n1_outlier", 7)
+        sh = seq_shard(S, rank, world)
+        xb = bits(full[:, :, sh.start : sh.start + sh.rows])
+        npart = sh.chunk_rows // 128
+        part = np.zeros((B * H, npart), dtype=np.int32)
+        for c in range(-(-sh.rows // 128)):
+            blk = xb[:, :, c * 128 : (c + 1) * 128].reshape(B * H, -1)
+            part[:, c] = oq.absmax_bits(blk, axis=1)
+        t = torch.from_numpy(part)
+        nccl_all_reduce_max()(t)
+        sc = oq.scale_from_amax_bits(t.numpy().max(axis=1).astype(np.uint16))
+        ref_sc = oq.per_bh_scale(bits(full))
+        assert np.array_equal(sc.view(np.uint32), ref_sc.view(np.uint32))
+        full8, _ = oq.quantize_with_scales(bits(full), oq.SCALE_PER_BH)
+        local8 = oq.quantize(xb, sc)
+        assert np.array_equal(local8, full8[:, :, sh.start : sh.start + sh.rows])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("S,world", [(300, 2), (1000, 3)])
+def test_per_bh_scales_combined_across_gloo_ranks(S, world):
+    mp.spawn(_bh_scale_worker, args=(world, _free_port(), S), nprocs=world, join=True)
+
+
+def test_per_bh_context_parallel_needs_a_reduce():
+    with pytest.raises(ValueError, match="all_reduce_max"):
+        ContextParallelAttention(1000, 0, 2, scale_mode=0)
