@@ -57,6 +57,7 @@ __device__ int g_trace_x = -1;
 __device__ int g_trace_y = -1;
 constexpr int kTraceSteps = 1024;  // events < 256
 __device__ __forceinline__ uint32_t* trace_target() {
+  // (the launch grid is 1-D: cta_x is the CTA index, cta_y must be 0)
   return (g_trace_buf != nullptr && (int)blockIdx.x == g_trace_x && (int)blockIdx.y == g_trace_y)
              ? g_trace_buf
              : nullptr;
@@ -232,6 +233,16 @@ __device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& 
   y1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
+// This CTA's work unit: (b,h) and column (a group of NQ query tiles, or one
+// query tile for the split-step form), from the launch's 1-D unit range.
+__device__ __forceinline__ int unit_bh(const AttnKernelParams& p) {
+  return (p.unit_base + static_cast<int>(blockIdx.x)) / p.units_per_bh;
+}
+__device__ __forceinline__ int unit_x(const AttnKernelParams& p) {
+  const int u = p.unit_base + static_cast<int>(blockIdx.x);
+  return u - (u / p.units_per_bh) * p.units_per_bh;
+}
+
 // Which K/V tile step j reads: chunk c, tile t within the chunk, valid rows.
 __device__ __forceinline__ void step_info(const AttnKernelParams& p, int j, int& c, int& t,
                                           int& valid, bool& extra) {
@@ -281,9 +292,9 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
                          const AttnKernelParams& p, const Bars& bar, uint8_t* smem, int n_steps) {
   using C = Cfg<NQ, PMODE, 1, false, DB>;
   RP_TRACE_INIT();
-  const int bh = blockIdx.y;
+  const int bh = unit_bh(p);
   // KS: one query tile per CTA, read by both tiles' QK MMAs from Q slot 0.
-  const int qt0 = KS ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * NQ;
+  const int qt0 = KS ? unit_x(p) : unit_x(p) * NQ;
   constexpr int kQTiles = KS ? 1 : NQ;
   auto load_q = [&]() {
     mbar_arrive_expect_tx(bar.q_full, kQTiles * C::kQBytes);
@@ -587,12 +598,12 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   const int row = wq * 32 + lane;
   const int col0 = half * NC;
   const bool tracer = (wq == 0 && lane == 0 && half == 0);
-  const int bh = blockIdx.y;
+  const int bh = unit_bh(p);
   // KS (one query tile, its K/V steps split between the two tiles' warpgroups):
   // warpgroup t takes steps t, t + 2, ... and warpgroup 1 hands its partial
   // row max and sum to warpgroup 0, which merges the two O accumulators.
   static_assert(!KS || (NQ == 2 && NSPLIT == 1 && TAB && DB == 1), "KS: two tiles, table, D 128");
-  const int q_tile = KS ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * NQ + t;
+  const int q_tile = KS ? unit_x(p) : unit_x(p) * NQ + t;
   const int j0 = KS ? t : 0;
   constexpr int kStepStride = KS ? 2 : 1;
   const int q_tile_c = min(q_tile, p.n_q_tiles - 1);
@@ -641,7 +652,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     // extra (decode) tile belongs to the CTA's only query tile (NQ == 1).
     constexpr int kN = C::kSoftmaxWarps * 32;
     float* red = reinterpret_cast<float*>(smem + C::kOffT);
-    const int qt0c = min(KS ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * NQ,
+    const int qt0c = min(KS ? unit_x(p) : unit_x(p) * NQ,
                          p.n_q_tiles - 1);
     uint32_t vb = 0;
     for (int j = threadIdx.x; j < n_steps; j += kN) {
@@ -1127,7 +1138,7 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
 
   int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
   if (p.causal) {
-    const int q_end = KS ? static_cast<int>(blockIdx.x) + 1 : static_cast<int>(blockIdx.x) * NQ + NQ;
+    const int q_end = KS ? unit_x(p) + 1 : unit_x(p) * NQ + NQ;
     const int last_row = min(p.Sq, q_end * kTile) - 1;
     n_steps = min(n_steps, last_row / kTile + 1);
   }
@@ -1181,7 +1192,18 @@ cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int 
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_release);
   }
-  const dim3 grid(KS ? p.n_q_tiles : (p.n_q_tiles + NQ - 1) / NQ, B * H);
+  // 1-D grid over work units (the whole problem unless the caller set a range)
+  AttnKernelParams pl = p;
+  int units = 0;
+  if (pl.units_per_bh == 0) {
+    pl.unit_base = 0;
+    pl.units_per_bh = KS ? p.n_q_tiles : (p.n_q_tiles + NQ - 1) / NQ;
+    units = pl.units_per_bh * B * H;
+  } else {
+    units = p.unit_count;
+  }
+  if (units <= 0) return cudaSuccess;
+  const dim3 grid(units, 1, 1);
   if (KS && decode_pdl_setting()) {
     // The decode may start while its quantize launch finishes (programmatic
     // dependent launch); its kernel waits for that launch before reading Q
@@ -1196,9 +1218,9 @@ cudaError_t launch_one(const AttnMaps& m, const AttnKernelParams& p, int B, int 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, m.q, m.k, m.v, m.kx, m.vx, m.o, p);
+    return cudaLaunchKernelEx(&cfg, kern, m.q, m.k, m.v, m.kx, m.vx, m.o, pl);
   }
-  kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(m.q, m.k, m.v, m.kx, m.vx, m.o, p);
+  kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(m.q, m.k, m.v, m.kx, m.vx, m.o, pl);
   return cudaGetLastError();
 }
 
@@ -1310,6 +1332,69 @@ extern "C" int rp_trace_setup(void* buf, int cta_x, int cta_y) {
 }
 #endif
 
+namespace {
+
+// Ragged-last-wave split (0, default; REPERCEP_B200_TAIL_SPLIT=1 turns it on,
+// read once).  Measured on B200 it neither helps nor hurts (Cosmos-shaped
+// shards of 8 / 16 / 64 (b,h): -0.5 / +1 / 0 %): a one-tile CTA takes about as
+// long as a two-tile one, because each softmax warp's own dependency chain,
+// not the SM's issue or pipe capacity, sets the time of a K/V step.
+int tail_split_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("REPERCEP_B200_TAIL_SPLIT");
+    return (e && std::atoi(e) == 1) ? 1 : 0;
+  }();
+  return v;
+}
+
+int attn_sm_count() {
+  static std::atomic<int> cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+// The two-tile CTAs of a launch fill whole waves of the GPU's SMs (one CTA per
+// SM) except the last; when that last wave is at most half full (r CTAs,
+// 0 < 2r <= SMs), its 2r query tiles run instead as one-tile CTAs after the
+// whole waves, each taking about half of a two-tile CTA's time.  A one-tile
+// CTA walks its K/V steps in the same order with the same per-step constants
+// as the tile does inside a two-tile CTA, so the output bits are those of the
+// single launch: that holds for non-causal attention (a causal CTA's step
+// count depends on its last tile) with one thread per row, and the split is
+// only made there.
+bool tail_split(const AttnKernelParams& p, int B, int H, int ep, int sp, int p_mode,
+                AttnKernelParams* main_p, AttnKernelParams* tail_p) {
+  if (!tail_split_setting() || p.causal || p.has_extra || sp != 1 || ep != kDefaultExpPoly ||
+      p.units_per_bh != 0)
+    return false;
+  const int ppb = (p.n_q_tiles + 1) / 2;
+  const int64_t units = (int64_t)ppb * B * H;
+  const int sms = attn_sm_count();
+  const int r = static_cast<int>(units % sms);
+  if (r == 0 || 2 * r > sms) return false;
+  (void)p_mode;
+  *main_p = p;
+  main_p->unit_base = 0;
+  main_p->units_per_bh = ppb;
+  main_p->unit_count = static_cast<int>(units - r);
+  // the tiles of the last r two-tile units, in (b,h)-major tile order
+  const int64_t first_tile = (units - r) / ppb * p.n_q_tiles + ((units - r) % ppb) * 2;
+  *tail_p = p;
+  tail_p->unit_base = static_cast<int>(first_tile);
+  tail_p->units_per_bh = p.n_q_tiles;
+  tail_p->unit_count = static_cast<int>((int64_t)B * H * p.n_q_tiles - first_tile);
+  return true;
+}
+
+}  // namespace
+
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& params, int B,
                              int H, int nq, int p_mode, int db, cudaStream_t st) {
   const int ep = exp_poly_setting();
@@ -1319,6 +1404,16 @@ cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& param
   p.rescale_tau = rescale_tau_setting();
   p.stagger = stagger_setting();
   p.mma_ahead = mma_ahead_setting();
+  if (nq == 2 && db == 1) {
+    AttnKernelParams pm, pt;
+    if (tail_split(p, B, H, ep, sp, p_mode, &pm, &pt)) {
+      cudaError_t e = (p_mode == 0) ? launch_variant<2, 0, kDefaultExpPoly, 1>(maps, pm, B, H, st)
+                                    : launch_variant<2, 1, 0, 1>(maps, pm, B, H, st);
+      if (e != cudaSuccess) return e;
+      return (p_mode == 0) ? launch_variant<1, 0, kDefaultExpPoly, 1>(maps, pt, B, H, st)
+                           : launch_variant<1, 1, 0, 1>(maps, pt, B, H, st);
+    }
+  }
   if (db == 2) {
     if (nq != 1) return cudaErrorInvalidValue;
     return (p_mode == 0) ? launch_variant<1, 0, 2, 1, 2>(maps, p, B, H, st)

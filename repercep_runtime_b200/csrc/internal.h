@@ -123,6 +123,12 @@ struct AttnKernelParams {
   // tile's P; 0 = every tile's QK(j), then every tile's PV(j - 1).
   int mma_ahead;
   int causal;
+  // Work units of a launch (1-D grid): CTA i takes unit u = unit_base + i,
+  // which is column u % units_per_bh (a group of NQ query tiles, or one query
+  // tile for the split-step form) of (b,h) u / units_per_bh.  units_per_bh 0:
+  // the whole problem (set by launch_attention).
+  int unit_base, units_per_bh;
+  int unit_count;        // units in this launch (host side)
   // Output: fp16 instead of bf16; out_plain = one unswizzled box of out_cols
   // (32 or 64) columns instead of 64-column swizzled boxes.
   int out_f16, out_plain, out_cols;

@@ -253,3 +253,22 @@ def test_attention_f16_matches_reference_kernel_golden():
         m = oa.parity_metrics(out.float().cpu().numpy(), ref)
         bound = 0.05 * m["max_ref"] if causal else MAX_ABS
         assert m["cos"] >= 0.999 and m["max_abs"] <= bound, (name, m)
+
+
+@pytest.mark.parametrize("p_mode", [0, 1])
+@pytest.mark.parametrize("mode", [oq.SCALE_PER_BH, oq.SCALE_PER_BLOCK128])
+def test_attention_is_batch_invariant(mode, p_mode):
+    """Every (b,h) slice has the same output bits whether it runs in a batch
+    of 10 (80 two-tile CTAs) or alone (8 two-tile units; with
+    REPERCEP_B200_TAIL_SPLIT=1, which the variants test sets, the launcher runs
+    those as 16 one-tile CTAs), also for a ragged S (odd tile count)."""
+    from repercep_runtime_b200 import ops
+
+    for S in (2048, 1900):
+        q, k, v = (gen_bf16((1, 10, S, 128), "n1", seed=s).cuda() for s in (81, 82, 83))
+        full = ops.fp8_attention(q, k, v, scale_mode=mode, p_mode=p_mode)
+        for h in (0, 3, 9):
+            one = ops.fp8_attention(q[:, h : h + 1].contiguous(), k[:, h : h + 1].contiguous(),
+                                    v[:, h : h + 1].contiguous(), scale_mode=mode, p_mode=p_mode)
+            torch.cuda.synchronize()
+            assert torch.equal(one.view(torch.int16), full[:, h : h + 1].view(torch.int16)), (S, h)

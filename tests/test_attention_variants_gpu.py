@@ -17,7 +17,9 @@ library reads these switches once per process):
 * REPERCEP_B200_MMA_AHEAD=1 -- per step, each tile's PV followed by its
   next-but-one QK (instead of every tile's QK, then every tile's PV);
 * REPERCEP_B200_STAGGER=3 -- ping-pong: tile 0's exp phase also waits for
-  tile 1's of the previous step.
+  tile 1's of the previous step;
+* REPERCEP_B200_TAIL_SPLIT=1 -- a last wave of two-tile CTAs at most half
+  full runs as one-tile CTAs instead.
 """
 
 from __future__ import annotations
@@ -47,6 +49,7 @@ SUITE = ["tests/test_attention_gpu.py", "tests/test_decode_gpu.py", "tests/test_
         "REPERCEP_B200_DECODE_PDL=0",
         "REPERCEP_B200_MMA_AHEAD=1",
         "REPERCEP_B200_STAGGER=3",
+        "REPERCEP_B200_TAIL_SPLIT=1",
     ],
 )
 def test_attention_suite_under_schedule_switch(switch):
