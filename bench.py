@@ -1064,6 +1064,9 @@ def main() -> None:
                     help="skip the side measurements (quantize bandwidth, SDPA and FP8 linear rows)")
     ap.add_argument("--no-graph", action="store_true", help="decode: launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--no-wan-cp", action="store_true", help="N > 1: skip the wan_cp record")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch (profiling a smaller case of the same kernel)")
+    ap.add_argument("--heads", type=int, default=None, help="override the workload's head count")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1071,7 +1074,13 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    for key, val in (("B", args.batch), ("H", args.heads)):
+        if val is not None:
+            if key not in w or val <= 0:
+                ap.error(f"--{'batch' if key == 'B' else 'heads'} does not apply to {args.workload}")
+            w[key] = val
+            w["desc"] += f" [{key} overridden to {val}]"
 
     if args.impl == "reference":
         run_reference_arm(args, w, rank, world)
