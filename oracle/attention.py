@@ -103,14 +103,16 @@ def reference_tile_loop(
     block_n: int = 128,
     fp8_max: float = 448.0,
     rescale_tau: float = 0.0,
+    rescale_group: int = 32,
 ) -> np.ndarray:
     """The reference kernel's FA-2 loop in fp32; returns (BH, Sq, D) fp32.
 
     ``rescale_tau`` = 0 is the reference loop.  A positive value models the
-    B200 kernel's rescale threshold (log2 units): within each group of 32
-    query rows the running max is raised only when some row's max would grow
-    by more than ``rescale_tau``; meanwhile p may reach 2^tau, so P is rounded
-    as e4m3(p * fp8_max * 2^-tau) and the PV product is scaled back by 2^tau.
+    B200 kernel's rescale threshold (log2 units): within each group of
+    ``rescale_group`` query rows (the rows one softmax warp holds) the running
+    max is raised only when some row's max would grow by more than
+    ``rescale_tau``; meanwhile p may reach 2^tau, so P is rounded as
+    e4m3(p * fp8_max * 2^-tau) and the PV product is scaled back by 2^tau.
     """
     BH, Sq, D = q8.shape
     Skv = k8.shape[1]
@@ -138,8 +140,9 @@ def reference_tile_loop(
             if rescale_tau > 0:
                 with np.errstate(invalid="ignore"):
                     need = m_cand > m + np.float32(rescale_tau * np.log(2.0))
-                need = np.concatenate([need, np.zeros((-Sq) % 32, dtype=bool)])
-                grp = np.repeat(need.reshape(-1, 32).any(axis=1), 32)[:Sq]
+                g = int(rescale_group)
+                need = np.concatenate([need, np.zeros((-Sq) % g, dtype=bool)])
+                grp = np.repeat(need.reshape(-1, g).any(axis=1), g)[:Sq]
                 m_new = np.where(grp, m_cand, m).astype(np.float32)
             else:
                 m_new = m_cand

@@ -40,11 +40,11 @@ constexpr int kTile = 128;
 constexpr int kTileBytes = kTile * kTile;
 constexpr int kKSt = 3;
 constexpr int kVSt = 3;
-constexpr int kDefaultExpPoly = 2;
-constexpr int kDefaultRowSplit = 1;
+constexpr int kDefaultExpPoly = 2;   // with row layouts 1 and 2 (the lane split: 0)
+constexpr int kLaneSplitExpPoly = 0;
+constexpr int kDefaultRowSplit = 3;  // kLaneSplit
 constexpr float kDefaultRescaleTau = 1.0f;
 constexpr int kDefaultStagger = 2;
-constexpr int kDefaultMmaAhead = 0;
 
 // Pipeline tracing (compiled in only with -DRP_PIPELINE_TRACE): one chosen CTA
 // records (SM clock, event << 16 | step) at every barrier hand-off of every
@@ -90,12 +90,24 @@ enum : int {
   kErrWaitStag = 0x10D,
 };
 
+// Row layouts of the softmax warps (NSPLIT):
+//   1  one thread per query row: warp w of a tile holds the 32 rows of TMEM
+//      lane quarter w, all 128 columns each (4 warps per tile);
+//   2  two warps per lane quarter, each row's columns split between them
+//      (64 each): row maxima and sums are swapped through shared memory;
+//   3  (kLaneSplit) two warps per lane quarter, 16 rows each, and each row's
+//      128 columns split between lanes t and t + 16 of its warp (64 each,
+//      tcgen05.ld 16x32bx2): row maxima and sums are combined with a shuffle.
+// 2 and 3 give 8 softmax warps per tile.
+constexpr int kLaneSplit = 3;
+
 // DB: head dim in 128-column blocks (1: D <= 128, the rows of D = 32 / 64
 // zero-padded to 128 bytes; 2: D = 256, one query tile per CTA).
 template <int NQ, int PMODE, int NSPLIT = 1, bool TAB = false, int DB = 1>
 struct Cfg {
-  static constexpr int kNC = kTile / NSPLIT;                 // S columns per softmax thread
-  static constexpr int kWarpsPerTile = 4 * NSPLIT;
+  static constexpr int kRowThreads = (NSPLIT == 1) ? 1 : 2;  // threads per query row
+  static constexpr int kNC = kTile / kRowThreads;            // S columns per softmax thread
+  static constexpr int kWarpsPerTile = 4 * kRowThreads;
   static constexpr int kSoftmaxWarps = kWarpsPerTile * NQ;
   static constexpr int kTmaWarp = kSoftmaxWarps;
   static constexpr int kMmaWarp = kSoftmaxWarps + 1;
@@ -104,6 +116,7 @@ struct Cfg {
   static constexpr int kPParts = (PMODE == 0) ? 1 : 2;
   static_assert(NQ * (1 + DB) * kTile <= 512, "TMEM holds S and O of every query tile");
   static_assert(DB == 1 || NSPLIT == 1, "row split only for D <= 128");
+  static_assert(NSPLIT >= 1 && NSPLIT <= 3, "row layouts 1, 2, 3");
   static constexpr int kTmemCols = (NQ * (1 + DB) * kTile > 256) ? 512 : 256;
   static constexpr int kSt = (DB == 2) ? 2 : 3;       // K and V ring stages (<= kKSt, kVSt)
   static constexpr int kQBytes = DB * kTileBytes;     // one query tile
@@ -581,10 +594,12 @@ __device__ void mma_issuer_ahead(const AttnKernelParams& p, const Bars& bar, uin
 }
 
 // ----------------------------------------------------------------- softmax
-// NSPLIT threads share each query row: thread (half, row) owns S columns
-// [half * kNC, half * kNC + kNC).  With NSPLIT = 2 the two halves swap their
-// partial row maxima through shared memory every step and their partial row
-// sums once at the end.
+// Row layout NSPLIT (see Cfg): 1, one thread per row owning all columns;
+// 2, thread (half, row) owns S columns [half * kNC, half * kNC + kNC) and the
+// two halves swap their partial row maxima through shared memory every step
+// and their partial row sums once at the end; 3 (kLaneSplit), warp half h of
+// lane quarter q holds rows q*32 + 16h + (lane & 15), lane owning columns
+// [64 (lane >> 4), +64), combined with a shuffle.
 template <int NQ, int PMODE, int EPOLY, int NSPLIT, bool TAB, int DB, bool KS = false>
 __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, const Bars& bar,
                            uint8_t* smem, uint32_t tmem, int n_steps) {
@@ -595,8 +610,9 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   const int t = warp / C::kWarpsPerTile;
   const int sub = warp % C::kWarpsPerTile;
   const int half = sub >> 2, wq = sub & 3;
-  const int row = wq * 32 + lane;
-  const int col0 = half * NC;
+  constexpr bool LS = (NSPLIT == kLaneSplit);
+  const int row = LS ? wq * 32 + half * 16 + (lane & 15) : wq * 32 + lane;
+  const int col0 = LS ? (lane >> 4) * NC : half * NC;
   const bool tracer = (wq == 0 && lane == 0 && half == 0);
   const int bh = unit_bh(p);
   // KS (one query tile, its K/V steps split between the two tiles' warpgroups):
@@ -607,9 +623,11 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   const int j0 = KS ? t : 0;
   constexpr int kStepStride = KS ? 2 : 1;
   const int q_tile_c = min(q_tile, p.n_q_tiles - 1);
-  const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-  const uint32_t tS = tmem + lane_base + t * kTile + col0;
-  const uint32_t tO = tmem + lane_base + (NQ + t * DB) * kTile + col0;
+  // TMEM addresses: the lane field is the warp's first lane; LS loads put
+  // the column offset of the upper 16 threads in the instruction (64).
+  const uint32_t lane_base = static_cast<uint32_t>(LS ? wq * 32 + half * 16 : wq * 32) << 16;
+  const uint32_t tS = tmem + lane_base + t * kTile + (LS ? 0 : col0);
+  const uint32_t tO = tmem + lane_base + (NQ + t * DB) * kTile + (LS ? 0 : col0);
   uint8_t* pbase = smem + C::kOffP + t * C::kPBuf * C::kPStride;
   // exchange slots: [t][parity 0,1 = row max, 2 = row sum][half][row]
   float* xch = reinterpret_cast<float*>(smem + C::kOffX) + t * 3 * 2 * kTile;
@@ -741,7 +759,12 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     tc_fence_after();
     uint32_t r[NC / 32][32];
 #pragma unroll
-    for (int q = 0; q < NC / 32; ++q) tmem_ld32(tS + 32 * q, r[q]);
+    for (int q = 0; q < NC / 32; ++q) {
+      if constexpr (LS)
+        tmem_ld16x2(tS + 32 * q, r[q]);
+      else
+        tmem_ld32(tS + 32 * q, r[q]);
+    }
     tmem_wait_ld();
 #pragma unroll
     for (int q = 0; q < NC / 32; ++q) reg_fence(r[q]);
@@ -787,6 +810,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     float mx = ach[0];
 #pragma unroll
     for (int k = 1; k < NCH; ++k) mx = fmaxf(mx, ach[k]);
+    if constexpr (LS) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));  // the row's other half
     if constexpr (NSPLIT == 2) {
       // swap partial maxima with the warp that owns the other half of these rows
       xch[((j & 1) * 2 + half) * kTile + row] = mx;
@@ -892,14 +916,14 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     constexpr int kChunks = NC / 16;  // 16-byte P chunks of this thread
 #pragma unroll
     for (int k = 0; k < kChunks; ++k) {
-      const int kg = half * kChunks + k;
+      const int kg = (LS ? (lane >> 4) : half) * kChunks + k;
       st_shared_v4(prow + ((kg ^ (row & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
                    pk[4 * k + 3]);
     }
     if constexpr (PMODE == 1) {
 #pragma unroll
       for (int k = 0; k < kChunks; ++k) {
-        const int kg = half * kChunks + k;
+        const int kg = (LS ? (lane >> 4) : half) * kChunks + k;
         st_shared_v4(prow + kTileBytes + ((kg ^ (row & 7)) << 4), pl[4 * k], pl[4 * k + 1],
                      pl[4 * k + 2], pl[4 * k + 3]);
       }
@@ -922,7 +946,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
 #pragma unroll
       for (int q = 0; q < DB * NC / 32; ++q) {
         uint32_t o[32];
-        tmem_ld32(tO + 32 * q, o);
+        if constexpr (LS)
+          tmem_ld16x2(tO + 32 * q, o);
+        else
+          tmem_ld32(tO + 32 * q, o);
         tmem_wait_ld();
         reg_fence(o);
 #pragma unroll
@@ -932,7 +959,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
           o[i] = __float_as_uint(u0);
           o[i + 1] = __float_as_uint(u1);
         }
-        tmem_st32(tO + 32 * q, o);
+        if constexpr (LS)
+          tmem_st16x2(tO + 32 * q, o);
+        else
+          tmem_st32(tO + 32 * q, o);
       }
       tmem_wait_st();
     }
@@ -955,6 +985,9 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   // unambiguous even though o_done phases were skipped above).
   if (ok && n_steps > 0)
     ok = warp_wait(bar.o_final + t, 0, bar.abort_flag, p.status, kErrWaitOFinal);
+  if constexpr (LS) {
+    if (ok) l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);  // the row's other half
+  }
   if (ok && NSPLIT == 2) {  // the two halves' row sums
     xch[(2 * 2 + half) * kTile + row] = l_run;
     __syncwarp();
@@ -1039,13 +1072,17 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     }
   } else {
 #pragma unroll
-    for (int hh = 0; hh < 2 * DB / NSPLIT; ++hh) {
-      const int box = (NSPLIT == 2) ? half : hh;  // 64-column box this thread fills
+    for (int hh = 0; hh < 2 * DB / C::kRowThreads; ++hh) {
+      // 64-column box this thread fills
+      const int box = LS ? (lane >> 4) : (NSPLIT == 2) ? half : hh;
       const uint32_t srow = smem_u32(stage_of(box)) + row * 128;
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         uint32_t o[32];
-        tmem_ld32(tO + 64 * hh + 32 * cc, o);
+        if constexpr (LS)
+          tmem_ld16x2(tO + 32 * cc, o);  // the thread's own 64-column half, 32 at a time
+        else
+          tmem_ld32(tO + 64 * hh + 32 * cc, o);
         tmem_wait_ld();
         reg_fence(o);
         merge_o(o, 64 * hh + 32 * cc);
@@ -1246,13 +1283,14 @@ cudaError_t launch_variant(const AttnMaps& m, const AttnKernelParams& p, int B, 
 }
 
 // Elements (of every 8) whose exp2 runs on the FMA pipe instead of MUFU.
-// REPERCEP_B200_EXP_POLY in {0, 2, 4} overrides the default (read once).
+// REPERCEP_B200_EXP_POLY in {0, 2, 4} overrides the default (read once);
+// -1 = the default of the row layout in use.
 int exp_poly_setting() {
   static const int v = [] {
     const char* e = std::getenv("REPERCEP_B200_EXP_POLY");
-    if (!e) return kDefaultExpPoly;
+    if (!e) return -1;
     const int x = std::atoi(e);
-    return (x == 0 || x == 2 || x == 4) ? x : kDefaultExpPoly;
+    return (x == 0 || x == 2 || x == 4) ? x : -1;
   }();
   return v;
 }
@@ -1269,13 +1307,14 @@ int decode_ksplit_setting() {
   return v;
 }
 
-// Threads per query row in the softmax warpgroups (1 or 2).
+// Softmax row layout (1, 2 or 3 = kLaneSplit, see Cfg).
 // REPERCEP_B200_ROW_SPLIT overrides the default (read once).
 int split_setting() {
   static const int v = [] {
     const char* e = std::getenv("REPERCEP_B200_ROW_SPLIT");
     if (!e) return kDefaultRowSplit;
-    return std::atoi(e) == 2 ? 2 : 1;
+    const int x = std::atoi(e);
+    return (x == 2 || x == kLaneSplit) ? x : 1;
   }();
   return v;
 }
@@ -1295,11 +1334,12 @@ int stagger_setting() {
 
 // MMA issue order of the attention kernel (1: each tile's PV(i) then its
 // QK(i + 2); 0: every tile's QK(j), then every tile's PV(j - 1)).
-// REPERCEP_B200_MMA_AHEAD overrides the default (read once).
+// REPERCEP_B200_MMA_AHEAD overrides the default (read once); -1 = the default
+// of the row layout in use (1 with the lane split, else 0).
 int mma_ahead_setting() {
   static const int v = [] {
     const char* e = std::getenv("REPERCEP_B200_MMA_AHEAD");
-    if (!e) return kDefaultMmaAhead;
+    if (!e) return -1;
     return std::atoi(e) != 0 ? 1 : 0;
   }();
   return v;
@@ -1397,13 +1437,17 @@ bool tail_split(const AttnKernelParams& p, int B, int H, int ep, int sp, int p_m
 
 cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& params, int B,
                              int H, int nq, int p_mode, int db, cudaStream_t st) {
-  const int ep = exp_poly_setting();
-  // the row split has no plain-output epilogue and no D = 256 form
-  const int sp = (params.out_plain || db != 1) ? 1 : split_setting();
+  // the row splits have no plain-output epilogue, no D = 256 and no hi/lo P form
+  const int sp = (params.out_plain || db != 1 || p_mode != 0) ? 1 : split_setting();
+  const bool lane_split = (nq == 2 && sp == kLaneSplit);
+  // measured defaults (Cosmos / cfg2 shapes on B200): the lane split runs
+  // every exp on MUFU and issues each tile's next QK right after its PV
+  const int ep_env = exp_poly_setting(), ahead_env = mma_ahead_setting();
+  const int ep = ep_env >= 0 ? ep_env : (lane_split ? kLaneSplitExpPoly : kDefaultExpPoly);
   AttnKernelParams p = params;
   p.rescale_tau = rescale_tau_setting();
   p.stagger = stagger_setting();
-  p.mma_ahead = mma_ahead_setting();
+  p.mma_ahead = ahead_env >= 0 ? ahead_env : (lane_split ? 1 : 0);
   if (nq == 2 && db == 1) {
     AttnKernelParams pm, pt;
     if (tail_split(p, B, H, ep, sp, p_mode, &pm, &pt)) {
@@ -1424,6 +1468,10 @@ cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& param
       if (ep == 0) return launch_variant<2, 0, 0, 2>(maps, p, B, H, st);
       if (ep == 4) return launch_variant<2, 0, 4, 2>(maps, p, B, H, st);
       return launch_variant<2, 0, 2, 2>(maps, p, B, H, st);
+    }
+    if (sp == kLaneSplit) {  // EXP_POLY 4 is not built for it: 2 instead
+      if (ep == 0) return launch_variant<2, 0, 0, kLaneSplit>(maps, p, B, H, st);
+      return launch_variant<2, 0, 2, kLaneSplit>(maps, p, B, H, st);
     }
     if (ep == 0) return launch_variant<2, 0, 0, 1>(maps, p, B, H, st);
     if (ep == 4) return launch_variant<2, 0, 4, 1>(maps, p, B, H, st);
