@@ -721,8 +721,9 @@ def dominant_roofline(w: dict, runner: Runner, kernel_ms: float, peaks: dict) ->
         return {"bound": "hbm", "achieved": algo / (kernel_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                 "frac": algo / (kernel_ms / 1e3) / 1e9 / peak, "traffic": profile_traffic("decode"),
                 "algorithmic_bytes": algo,
-                "kernel": ("fa8_fwd_kernel<2,0,2,1,1,1,1> (prefix decode, K/V steps split between two softmax "
-                           "warpgroups)" if runner.args.p_mode == 0 else "fa8_fwd_kernel<1,1> (prefix decode)"),
+                "kernel": ("fa8_fwd_kernel<2,0,0,3,1,1,1> (prefix decode, K/V steps split between two softmax "
+                           "warpgroups, two lanes per row)" if runner.args.p_mode == 0
+                           else "fa8_fwd_kernel<1,1> (prefix decode)"),
                 "peak_source": "of measured" if "hbm_gbs" in peaks else "of fallback"}
     if "bf16_tflops_sustained" in peaks:
         peak = 2.0 * float(peaks["bf16_tflops_sustained"])

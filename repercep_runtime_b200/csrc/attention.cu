@@ -618,7 +618,8 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   // KS (one query tile, its K/V steps split between the two tiles' warpgroups):
   // warpgroup t takes steps t, t + 2, ... and warpgroup 1 hands its partial
   // row max and sum to warpgroup 0, which merges the two O accumulators.
-  static_assert(!KS || (NQ == 2 && NSPLIT == 1 && TAB && DB == 1), "KS: two tiles, table, D 128");
+  static_assert(!KS || (NQ == 2 && (NSPLIT == 1 || NSPLIT == kLaneSplit) && TAB && DB == 1),
+                "KS: two tiles, one thread or two lanes per row, table, D 128");
   const int q_tile = KS ? unit_x(p) : unit_x(p) * NQ + t;
   const int j0 = KS ? t : 0;
   constexpr int kStepStride = KS ? 2 : 1;
@@ -1027,7 +1028,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     if constexpr (KS) {
       if (has1) {
         uint32_t o1[32];
-        tmem_ld32(tO + DB * kTile + col, o1);  // tile 1's accumulator
+        if constexpr (LS)  // tile 1's accumulator, this thread's half row
+          tmem_ld16x2(tO + DB * kTile + col, o1);
+        else
+          tmem_ld32(tO + DB * kTile + col, o1);  // tile 1's accumulator
         tmem_wait_ld();
         reg_fence(o1);
 #pragma unroll
@@ -1481,8 +1485,12 @@ cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& param
   if (nq == 1 && p_mode == 0) {
     const int n_steps = p.n_main_tiles + (p.has_extra ? 1 : 0);
     if (decode_ksplit_setting() && step_table_setting() && !p.causal &&
-        n_steps <= Cfg<2, 0, 1, true, 1>::kTableSteps)
+        n_steps <= Cfg<2, 0, 1, true, 1>::kTableSteps) {
+      // the lane split (its default: every exp on MUFU) or one thread per row
+      if (split_setting() == kLaneSplit && !p.out_plain)
+        return launch_one<2, 0, 0, kLaneSplit, true, 1, true>(maps, p, B, H, st);
       return launch_one<2, 0, 2, 1, true, 1, true>(maps, p, B, H, st);
+    }
     return launch_variant<1, 0, 2, 1>(maps, p, B, H, st);
   }
   if (nq == 1 && p_mode == 1) return launch_variant<1, 1, 0, 1>(maps, p, B, H, st);
