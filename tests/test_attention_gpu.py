@@ -174,16 +174,19 @@ def test_attention_cfg2_sampled(p_mode):
 
 
 def test_attention_cosmos_sampled():
-    """Cosmos shape: B=2 H=32 S=57600, N(0,0.5), per-128-block scales."""
-    rows = np.r_[0:64, 30000:30064, 57536:57600]
-    _sampled_parity(2, 32, 57600, "n05", oq.SCALE_PER_BLOCK128, 0, rows, [0, 63], False)
+    """Cosmos shape: B=2 H=32 S=57600, N(0,0.5), per-128-block scales; five
+    (b,h) slices across both batches, rows at the start, in three 128-row
+    tiles inside and at the end."""
+    rows = np.r_[0:64, 12800:12864, 30000:30064, 45100:45164, 57536:57600]
+    _sampled_parity(2, 32, 57600, "n05", oq.SCALE_PER_BLOCK128, 0, rows, [0, 17, 31, 40, 63], False)
 
 
 def test_attention_wan_sampled():
     """Wan shape: B=2 H=40 S=75600 (590 full blocks + an 80-token one),
-    per-block scales; rows at the start, middle and in the ragged last block."""
+    per-block scales; four slices, rows at the start, middle and in the
+    ragged last block."""
     rows = np.r_[0:32, 40000:40032, 75520:75600]
-    _sampled_parity(2, 40, 75600, "n05", oq.SCALE_PER_BLOCK128, 0, rows, [0, 79], False)
+    _sampled_parity(2, 40, 75600, "n05", oq.SCALE_PER_BLOCK128, 0, rows, [0, 23, 52, 79], False)
 
 
 HEAD_DIM_CASES = [
