@@ -869,8 +869,9 @@ def wan_cp_record(args, rank: int, world: int, dev, stream) -> dict | None:  # t
         fl = flops_per_call(w)
         record = {
             "workload": "wan", "desc": w["desc"], "n_gpus": world,
-            "parallelism": f"context-parallel x{world} (NCCL all-gather of e4m3 K/V + scales, "
-                           f"{CP_CHUNKS} overlapped (b,h) chunks)",
+            "parallelism": f"context-parallel x{world} (NCCL all-gather of e4m3 K/V + scales in (b,h) "
+                           f"chunks: a first chunk of one CTA wave, then {CP_CHUNKS} whole-wave chunks, each "
+                           f"chunk's attention overlapping the later chunks' gathers)",
             "ms_per_call": cp_ms, "tflops": fl / (cp_ms / 1e3) / 1e12,
             "tflops_per_gpu": fl / (cp_ms / 1e3) / 1e12 / world,
             "quantize_ms": quant_ms, "attention_ms": attn_ms,

@@ -93,10 +93,37 @@ AllGather = Callable[["object", "object"], None]  # (output, input) -> None
 
 # (b, h) chunks per device call: every chunk's K/V gather is issued up front
 # and its attention starts as soon as that gather lands, so all gathers but
-# the first run under attention.  Measured on Wan (B2 H40 S75600), max over
-# ranks: 8 GPUs 21.95 ms unchunked, 21.25 with 2 chunks, 21.26 with 4; 2 GPUs
-# 81.15 / 80.84 / 81.98 (8 chunks).
+# the first run under attention.  Even splits measured on Wan (B2 H40 S75600),
+# max over ranks: 8 GPUs 21.95 ms unchunked, 21.25 with 2 chunks, 21.26 with 4;
+# 2 GPUs 81.15 / 80.84 / 81.98 (8 chunks).  The default plan (cp_chunk_bounds)
+# makes the first chunk about one wave of CTAs, so the one gather nothing
+# overlaps is small, and cuts the rest into CP_CHUNKS chunks of whole waves.
 CP_CHUNKS = 2
+
+
+def cp_chunk_bounds(bh: int, q_tiles: int, sms: int = 148, later: int = CP_CHUNKS) -> list[tuple[int, int]]:
+    """(b, h) ranges of the overlapped context-parallel call.
+
+    A (b, h) slice of this rank's queries is ceil(q_tiles / 2) two-tile CTAs.
+    The first range holds the slices that fill one wave of ``sms`` CTAs (at
+    least one), so its gather -- the only one no attention overlaps -- moves
+    a small part of K/V; the rest is cut into ``later`` ranges whose sizes are
+    multiples of that wave, so no launch ends on a ragged wave."""
+    if bh <= 0:
+        return []
+    pairs = max(1, -(-q_tiles // 2))
+    wave = max(1, sms // pairs)
+    first = min(wave, bh)
+    bounds = [(0, first)]
+    rest = bh - first
+    if rest > 0:
+        step = -(-rest // max(1, later))
+        step = -(-step // wave) * wave
+        a = first
+        while a < bh:
+            bounds.append((a, min(bh, a + step)))
+            a += step
+    return bounds
 
 
 def nccl_all_reduce_max(group=None):  # type: ignore[no-untyped-def]
@@ -321,9 +348,10 @@ class ContextParallelAttention:
     def attend_quantized(self, qq, kq, vq, out=None, chunks: int | None = None):  # type: ignore[no-untyped-def]
         """Gather K/V and attend, for quantized (per-128-block) shards.
 
-        The (b, h) range is cut into ``chunks`` (default CP_CHUNKS) when the
-        bound all_gather is asynchronous: every chunk's gathers are issued
-        first, and chunk i's attention waits only for chunk i's gathers."""
+        When the bound all_gather is asynchronous the (b, h) range is cut into
+        chunks -- ``cp_chunk_bounds``'s plan by default, or ``chunks`` even
+        parts -- every chunk's gathers are issued first, and chunk i's
+        attention waits only for chunk i's gathers."""
         import torch
 
         from repercep_runtime_b200 import ops
@@ -333,8 +361,13 @@ class ContextParallelAttention:
         bh = B * H
         k8 = kq.data.view(torch.uint8).reshape(bh, rows, D)
         v8 = vq.data.view(torch.uint8).reshape(bh, rows, D)
-        n = CP_CHUNKS if chunks is None else chunks
-        n = min(n, bh) if getattr(self.all_gather, "supports_async", False) else 1
+        if chunks is None:
+            sms = torch.cuda.get_device_properties(qq.data.device).multi_processor_count
+            bounds = cp_chunk_bounds(bh, -(-rows // BLOCK), sms)
+        else:
+            n = max(1, min(chunks, bh))
+            bounds = [(i * bh // n, (i + 1) * bh // n) for i in range(n)]
+        n = len(bounds) if getattr(self.all_gather, "supports_async", False) else 1
         if out is None:
             out = torch.empty((B, H, rows, D), dtype=torch.bfloat16, device=qq.data.device)
         if not out.is_contiguous():
@@ -344,7 +377,6 @@ class ContextParallelAttention:
             return ops.attention_fp8_chunked(qq, k_all.view(ops.FP8), v_all.view(ops.FP8), ks_all,
                                              vs_all, last_rows=sh.last_rows, scale=self.scale,
                                              p_mode=self.p_mode, out=out)
-        bounds = [(i * bh // n, (i + 1) * bh // n) for i in range(n)]
         ks = kq.scales.reshape(bh, -1)
         vs = vq.scales.reshape(bh, -1)
         pending = [self._gather(k8[a:b], v8[a:b], ks[a:b], vs[a:b], async_op=True) for a, b in bounds]
@@ -366,6 +398,7 @@ __all__ = [
     "CP_CHUNKS",
     "ContextParallelAttention",
     "SeqShard",
+    "cp_chunk_bounds",
     "nccl_all_gather",
     "nccl_all_reduce_max",
     "seq_shard",

@@ -187,3 +187,19 @@ def test_per_bh_scales_combined_across_gloo_ranks(S, world):
 def test_per_bh_context_parallel_needs_a_reduce():
     with pytest.raises(ValueError, match="all_reduce_max"):
         ContextParallelAttention(1000, 0, 2, scale_mode=0)
+
+
+@pytest.mark.parametrize("bh,rows,first,sizes", [
+    (80, 9450, 4, [4, 40, 36]),     # Wan over 8 ranks: 37 two-tile CTAs per slice, 4 slices a wave
+    (80, 18900, 2, [2, 40, 38]),    # 4 ranks: 74 per slice
+    (80, 37800, 1, [1, 40, 39]),    # 2 ranks: 148 per slice, one slice a wave
+    (3, 300, 3, [3]),               # everything fits in the first wave
+    (1, 75600, 1, [1]),
+])
+def test_cp_chunk_plan(bh, rows, first, sizes):
+    from repercep_runtime_b200.parallel import cp_chunk_bounds
+
+    b = cp_chunk_bounds(bh, -(-rows // 128))
+    assert [y - x for x, y in b] == sizes
+    assert b[0] == (0, first)
+    assert b[0][0] == 0 and b[-1][1] == bh and all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
