@@ -10,12 +10,16 @@ What changes is the layout handling: diffusers passes (B, S, H, D) and the
 B200 kernels read and write that layout through strides, so the reference's
 three ``permute(0, 2, 1, 3).contiguous()`` copies in and one out (:264-267,
 :286) are gone.  The reference's non-finite guard (``isfinite().all()`` per
-call, :271-285, falling back to SDPA for that call) is kept by default because
-it is part of the seam's contract, and it costs a host synchronisation per
-call.  ``REPERCEP_B200_FINITE_GUARD=deferred`` keeps the check on the device
-instead: every call adds "any non-finite output" to a per-device counter
-without synchronising, and ``nonfinite_calls()`` reads it (once per denoise
-step, say); ``REPERCEP_B200_FINITE_GUARD=0`` drops the check.
+call, :271-285, falling back to SDPA for that call) costs a host
+synchronisation per call; by default the check stays on the device instead:
+every call adds "any non-finite output" to a per-device counter without
+synchronising, and ``nonfinite_calls()`` reads it (once per denoise step, say).
+The FP8 path turns finite inputs into finite outputs (the quantizer saturates
+at the e4m3 range and the softmax is computed against the running max), so a
+non-finite output comes from a non-finite input, where the SDPA fallback is
+non-finite too.  ``REPERCEP_B200_FINITE_GUARD=sync`` (or ``1``) restores the
+reference's per-call check and fallback; ``REPERCEP_B200_FINITE_GUARD=0`` drops
+the check.
 
 Registration: the ``"repercep_fp8"`` entry of diffusers' registry is set to
 this module's function even when the reference's module registered first
@@ -43,10 +47,10 @@ _NONFINITE: dict[Any, Any] = {}
 
 
 def _guard_mode() -> str:
-    raw = os.environ.get("REPERCEP_B200_FINITE_GUARD", "1").strip().lower()
+    raw = os.environ.get("REPERCEP_B200_FINITE_GUARD", "deferred").strip().lower()
     if raw in ("0", "off", "false"):
         return "off"
-    return "deferred" if raw == "deferred" else "sync"
+    return "sync" if raw in ("1", "sync", "on", "true") else "deferred"
 
 
 def record_nonfinite(out: Any) -> None:

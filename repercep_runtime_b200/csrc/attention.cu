@@ -1415,8 +1415,10 @@ int attn_sm_count() {
 // only made there.
 bool tail_split(const AttnKernelParams& p, int B, int H, int ep, int sp, int p_mode,
                 AttnKernelParams* main_p, AttnKernelParams* tail_p) {
-  if (!tail_split_setting() || p.causal || p.has_extra || sp != 1 || ep != kDefaultExpPoly ||
-      p.units_per_bh != 0)
+  // the two-tile and one-tile instances built for it: one thread per row with
+  // the default exp split, or the lane split with every exp on MUFU
+  const bool built = (sp == 1 && ep == kDefaultExpPoly) || (sp == kLaneSplit && ep == kLaneSplitExpPoly);
+  if (!tail_split_setting() || p.causal || p.has_extra || !built || p.units_per_bh != 0)
     return false;
   const int ppb = (p.n_q_tiles + 1) / 2;
   const int64_t units = (int64_t)ppb * B * H;
@@ -1455,11 +1457,17 @@ cudaError_t launch_attention(const AttnMaps& maps, const AttnKernelParams& param
   if (nq == 2 && db == 1) {
     AttnKernelParams pm, pt;
     if (tail_split(p, B, H, ep, sp, p_mode, &pm, &pt)) {
-      cudaError_t e = (p_mode == 0) ? launch_variant<2, 0, kDefaultExpPoly, 1>(maps, pm, B, H, st)
-                                    : launch_variant<2, 1, 0, 1>(maps, pm, B, H, st);
-      if (e != cudaSuccess) return e;
-      return (p_mode == 0) ? launch_variant<1, 0, kDefaultExpPoly, 1>(maps, pt, B, H, st)
-                           : launch_variant<1, 1, 0, 1>(maps, pt, B, H, st);
+      cudaError_t e;
+      if (p_mode != 0) {
+        e = launch_variant<2, 1, 0, 1>(maps, pm, B, H, st);
+        return e != cudaSuccess ? e : launch_variant<1, 1, 0, 1>(maps, pt, B, H, st);
+      }
+      if (sp == kLaneSplit) {
+        e = launch_variant<2, 0, kLaneSplitExpPoly, kLaneSplit>(maps, pm, B, H, st);
+        return e != cudaSuccess ? e : launch_variant<1, 0, kLaneSplitExpPoly, kLaneSplit>(maps, pt, B, H, st);
+      }
+      e = launch_variant<2, 0, kDefaultExpPoly, 1>(maps, pm, B, H, st);
+      return e != cudaSuccess ? e : launch_variant<1, 0, kDefaultExpPoly, 1>(maps, pt, B, H, st);
     }
   }
   if (db == 2) {

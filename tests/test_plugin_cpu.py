@@ -180,3 +180,7 @@ def test_deferred_finite_guard_counts_without_sync(monkeypatch):
     assert db._guard_mode() == "off"
     monkeypatch.setenv("REPERCEP_B200_FINITE_GUARD", "1")
     assert db._guard_mode() == "sync"
+    monkeypatch.setenv("REPERCEP_B200_FINITE_GUARD", "sync")
+    assert db._guard_mode() == "sync"
+    monkeypatch.delenv("REPERCEP_B200_FINITE_GUARD")
+    assert db._guard_mode() == "deferred"  # the device-side check is the default
