@@ -739,48 +739,63 @@ def dominant_roofline(w: dict, runner: Runner, kernel_ms: float, peaks: dict) ->
 def decode_record(args, dev, stream, peaks: dict) -> dict:  # type: ignore[no-untyped-def]
     """The shared-prefix decode (token-VLA config) on this GPU, outside the
     timed region: one decode step (quantize the new queries and suffix K/V,
-    then the decode kernel) and the kernel alone, each captured once as a
-    CUDA graph and replayed, timed per replay with CUDA events."""
+    then the decode kernel) and the kernel alone, captured as CUDA graphs and
+    replayed, timed with CUDA events.
+
+    ``step_us`` / ``kernel_us``: per call, ten calls captured in one graph (a
+    decode loop captured whole, so one graph launch is shared by ten calls);
+    ``*_graph1``: one call per graph, back to back (each call also pays a
+    graph launch, ~1.7 us on B200); ``*_isolated``: the one-call graph, each
+    replay bracketed by its own events."""
     import torch
 
     w = WORKLOADS["decode"]
     r = Runner(args, w, 0, 1, dev)
     for _ in range(3):
         r.step()
-    g_step, g_kernel = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_step):
-        r.step()
     qq, kx, vx = r.quantized_suffix()
-    with torch.cuda.graph(g_kernel):
-        r.decode_kernel(qq, kx, vx)
-    n = 50
+    calls = {"step": r.step, "kernel": lambda: r.decode_kernel(qq, kx, vx)}
+    per_graph, n_calls = 10, 200
     out = {}
-    for name, g in (("step_us", g_step), ("kernel_us", g_kernel)):
-        for _ in range(5):
-            g.replay()
-        # back to back: n replays between two events (a decode loop's rate)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(n):
-            g.replay()
-        b.record(stream)
-        # isolated: each replay bracketed by its own events (includes their overhead)
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for c, d in evs:
-            c.record(stream)
-            g.replay()
-            d.record(stream)
-        torch.cuda.synchronize(dev)
-        out[name] = 1e3 * a.elapsed_time(b) / n
-        out[name + "_isolated"] = 1e3 * statistics.median(c.elapsed_time(d) for c, d in evs)
+    graphs = []
+    for name, fn in calls.items():
+        for per, key in ((per_graph, f"{name}_us"), (1, f"{name}_us_graph1")):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(per):
+                    fn()
+            graphs.append(g)
+            for _ in range(5):
+                g.replay()
+            n = n_calls // per
+            # back to back: n replays between two events (a decode loop's rate)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(n):
+                g.replay()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            out[key] = 1e3 * a.elapsed_time(b) / (n * per)
+            if per == 1:
+                # isolated: each replay bracketed by its own events (includes their overhead)
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                       for _ in range(50)]
+                for c, d in evs:
+                    c.record(stream)
+                    g.replay()
+                    d.record(stream)
+                torch.cuda.synchronize(dev)
+                out[f"{name}_us_isolated"] = 1e3 * statistics.median(c.elapsed_time(d) for c, d in evs)
     roof = dominant_roofline(w, r, out["kernel_us"] / 1e3, peaks)
-    del g_step, g_kernel
+    del graphs
     return {"workload": "decode", "desc": w["desc"], **out,
             "tflops": flops_per_call(w) / (out["kernel_us"] / 1e6) / 1e12,
             "achieved_gbs": roof["achieved"], "peak_gbs": roof["peak"], "frac": roof["frac"],
             "algorithmic_bytes": roof["algorithmic_bytes"], "kernel": roof["kernel"],
-            "timing": f"{n} CUDA-graph replays back to back between two CUDA events (*_us), and the "
-                      f"median of {n} replays each bracketed by its own events (*_isolated)"}
+            "timing": f"*_us: {n_calls} calls as {n_calls // per_graph} replays of a CUDA graph holding "
+                      f"{per_graph} calls, back to back between two CUDA events; *_us_graph1: {n_calls} "
+                      f"replays of a one-call graph; *_isolated: median of 50 one-call replays each "
+                      f"bracketed by its own events"}
 
 
 def wan_cp_record(args, rank: int, world: int, dev, stream) -> dict | None:  # type: ignore[no-untyped-def]

@@ -134,14 +134,14 @@ struct Cfg {
   static constexpr int kTableSteps = TAB ? ((NSPLIT == 2) ? 1536 : 2048) : 0;
   static constexpr int kTabBytes = TAB ? 64 + kTableSteps * 16 : 0;
   static constexpr int kOffBar = kOffT + kTabBytes;
-  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ + 32;
+  static constexpr int kNumBars = 1 + 2 * kKSt + 2 * kVSt + 7 * NQ + 1 + 12 * NQ + 32 + NQ;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Bars {
   uint64_t *q_full, *k_full, *k_empty, *v_full, *v_empty;
-  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *xch, *stag, *stag1;
+  uint64_t *s_full, *s_free, *p_full, *o_done, *o_final, *epi, *fin, *xch, *stag, *stag1, *epi2;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -165,7 +165,8 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   b.xch = b.fin + 1;  // [NQ][4 lane quarters][3]: row-max (x2 by step parity), row-sum
   b.stag = b.xch + 12 * NQ;  // [4 lane quarters][4 by step mod 4]: tile 0 exp done
   b.stag1 = b.stag + 16;     // [4 lane quarters][4 by step mod 4]: tile 1 exp done
-  b.tmem_slot = reinterpret_cast<uint32_t*>(b.stag1 + 16);
+  b.epi2 = b.stag1 + 16;     // [NQ] (decode) warpgroup's half of the output staged
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.epi2 + NQ);
   b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
   return b;
 }
@@ -197,10 +198,28 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+// Four floats to e4m3 (satfinite, round to nearest even), byte i = value i.
+// pack_e4m3x4: the two pair conversions write 16-bit halves that one mov
+// joins; built from the 16-bit results with a shift and an OR instead
+// (pack_e4m3x4_or), the step loop of the all-MUFU kernels ran ~2 % slower
+// (extra integer instructions on the softmax warps' issue path).  The
+// polynomial-exp and two-part-P kernels keep the OR form: with the joined
+// form ptxas spills registers in them.
+__device__ __forceinline__ uint32_t pack_e4m3x4_or(float a, float b, float c, float d) {
   const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
   const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
   return lo | (hi << 16);
+}
+
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  uint32_t r;
+  asm("{\n .reg .b16 lo, hi;\n"
+      " cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n"
+      " cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
+      " mov.b32 %0, {lo, hi};\n}"
+      : "=r"(r)
+      : "f"(a), "f"(b), "f"(c), "f"(d));
+  return r;
 }
 
 // Residual of four values after their e4m3 rounding in `packed`, re-packed.
@@ -212,7 +231,7 @@ __device__ __forceinline__ uint32_t pack_e4m3x4_residual(uint32_t packed, float 
       __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(packed >> 16), __NV_E4M3);
   const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
   const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-  return pack_e4m3x4(a - f01.x, b - f01.y, c - f23.x, d - f23.y);
+  return pack_e4m3x4_or(a - f01.x, b - f01.y, c - f23.x, d - f23.y);
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
@@ -323,7 +342,9 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
   // have written any operand, the prefix included.  What overlaps it is this
   // CTA's launch, barrier and TMEM setup.
   if (KS) griddep_wait();
+  RP_TRACE(82, 0);
   load_q();
+  RP_TRACE(83, 0);
 
   int nk = 0, nv = 0;
   bool ok = true;
@@ -637,6 +658,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   // KS (the decode): Q's scale and the suffix scales come from the launch
   // this one may overlap; wait for it before the first read.
   if constexpr (KS) griddep_wait();
+  if (tracer) RP_TRACE(210 + t, 0);  // softmax: predecessor complete
   const float sq = p.qs[bh * p.qs_bh + q_tile_c * p.qs_blk];
 
   // Largest V scale this CTA meets (positive floats order like their bits),
@@ -664,15 +686,47 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     l_out = __log2f(kj);
     i_out = __fdividef(1.f, kj);
   };
-  float4* const tab = reinterpret_cast<float4*>(smem + C::kOffT + 64);
+  float4* tab = reinterpret_cast<float4*>(smem + C::kOffT + 64);
   float4 cst_n = make_float4(0.f, 0.f, 0.f, 0.f);
-  if constexpr (TAB) {
+  // The decode (KS) with at most 32 steps: every softmax warp builds its own
+  // copy of the table, lane j holding step j, so the latency-bound prologue
+  // has no barrier across warps; the values are those of the shared table
+  // below.  (The long-sequence kernels keep the shared table: the per-warp
+  // form costs them registers.)
+  static_assert(!TAB || C::kSoftmaxWarps * 32 <= C::kTableSteps, "per-warp tables fit");
+  const int qt0c = min(KS ? unit_x(p) : unit_x(p) * NQ, p.n_q_tiles - 1);
+  if (KS && n_steps <= 32) {
+    float sk = 0.f, sv = 0.f;
+    if (lane < n_steps) {
+      int c, tt, valid;
+      bool extra;
+      step_info(p, lane, c, tt, valid, extra);
+      if (extra) {
+        const int idx = bh * p.kvx_bh + qt0c * p.kvx_blk;
+        sk = p.ksx[idx];
+        sv = p.vsx[idx];
+      } else {
+        const int64_t idx = c * p.kv_chunk + bh * p.kv_bh + tt * p.kv_blk;
+        sk = p.ks[idx];
+        sv = p.vs[idx];
+      }
+    }
+    const uint32_t vb = __reduce_max_sync(0xffffffffu, __float_as_uint(sv));
+    if (tracer) RP_TRACE(212 + t, 0);  // scale loads back
+    sv_max = __uint_as_float(vb);
+    inv_svmax = 1.f / sv_max;
+    tab += warp * 32;
+    if (lane < n_steps) {
+      const float kj = 448.f * sv * inv_svmax;
+      tab[lane] = make_float4(p.sm_scale_log2 * sk, __log2f(kj), __fdividef(1.f, kj), 0.f);
+    }
+    __syncwarp();
+    if (n_steps > j0) cst_n = tab[j0];
+  } else if constexpr (TAB) {
     // All softmax threads fill the table once (n_steps <= kTableSteps); the
     // extra (decode) tile belongs to the CTA's only query tile (NQ == 1).
     constexpr int kN = C::kSoftmaxWarps * 32;
     float* red = reinterpret_cast<float*>(smem + C::kOffT);
-    const int qt0c = min(KS ? unit_x(p) : unit_x(p) * NQ,
-                         p.n_q_tiles - 1);
     uint32_t vb = 0;
     for (int j = threadIdx.x; j < n_steps; j += kN) {
       int c, tt, valid;
@@ -692,8 +746,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       vb = max(vb, __float_as_uint(sv));
     }
     vb = __reduce_max_sync(0xffffffffu, vb);
+    if (tracer) RP_TRACE(212 + t, 0);  // scale loads back
     if (lane == 0) red[warp] = __uint_as_float(vb);
     named_bar_sync(1, kN);
+    if (tracer) RP_TRACE(214 + t, 0);
     vb = 0;
 #pragma unroll
     for (int w = 0; w < C::kSoftmaxWarps; ++w) vb = max(vb, __float_as_uint(red[w]));
@@ -876,8 +932,13 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       const uint64_t e8 = fadd2(fadd2(pack_f32x2(e[0], e[1]), pack_f32x2(e[2], e[3])),
                                 fadd2(pack_f32x2(e[4], e[5]), pack_f32x2(e[6], e[7])));
       sacc[i & 3] = (i < 4) ? e8 : fadd2(sacc[i & 3], e8);
-      pk[2 * i] = pack_e4m3x4(e[0], e[1], e[2], e[3]);
-      pk[2 * i + 1] = pack_e4m3x4(e[4], e[5], e[6], e[7]);
+      if constexpr (EPOLY == 0 && PMODE == 0) {
+        pk[2 * i] = pack_e4m3x4(e[0], e[1], e[2], e[3]);
+        pk[2 * i + 1] = pack_e4m3x4(e[4], e[5], e[6], e[7]);
+      } else {
+        pk[2 * i] = pack_e4m3x4_or(e[0], e[1], e[2], e[3]);
+        pk[2 * i + 1] = pack_e4m3x4_or(e[4], e[5], e[6], e[7]);
+      }
       if constexpr (PMODE == 1) {
         pl[2 * i] = pack_e4m3x4_residual(pk[2 * i], e[0], e[1], e[2], e[3]);
         pl[2 * i + 1] = pack_e4m3x4_residual(pk[2 * i + 1], e[4], e[5], e[6], e[7]);
@@ -998,59 +1059,69 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
   if (!ok) return;
 
-  // KS: warpgroup 1 hands its row max (the reference point of its O and l)
-  // and row sum to warpgroup 0 through the unused Q slot 1; warpgroup 0
-  // weights the two accumulators by 2^(m_t - max) and stores the result.
+  // KS: the two warpgroups swap their row max (the reference point of their
+  // O and l) and row sum through the unused Q slot 1; each then weights the
+  // two accumulators by 2^(m_t - max) for half of the output columns (32 of
+  // each thread's 64, or of each 64-column box), staged in tile 0's buffers.
   float w0 = 1.f, w1 = 0.f;
   bool has1 = false;
   if constexpr (KS) {
-    float* ml = reinterpret_cast<float*>(smem + C::kOffQ + C::kQBytes);
+    float* ml = reinterpret_cast<float*>(smem + C::kOffQ + C::kQBytes);  // [t][m, l][row]
     const float mu = (m_run == -INFINITY) ? 0.f : m_run;
-    if (t == 1) {
-      ml[row] = mu;
-      ml[kTile + row] = l_run;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar.epi + 1);
-      return;
-    }
-    if (!warp_wait(bar.epi + 1, 0, bar.abort_flag, p.status, kErrWaitEpi)) return;
+    ml[(2 * t) * kTile + row] = mu;
+    ml[(2 * t + 1) * kTile + row] = l_run;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar.epi + t);
+    if (!warp_wait(bar.epi + (1 - t), 0, bar.abort_flag, p.status, kErrWaitEpi)) return;
+    const float m0 = ml[row], l0 = ml[kTile + row];
     has1 = n_steps > 1;  // warpgroup 1 ran at least one step (else its O was never written)
+    l_run = l0;
     if (has1) {
-      const float mu1 = ml[row], l1 = ml[kTile + row];
-      const float mm = fmaxf(mu, mu1);
-      w0 = ex2_approx(mu - mm);
-      w1 = ex2_approx(mu1 - mm);
-      l_run = l_run * w0 + l1 * w1;
+      const float m1 = ml[2 * kTile + row], l1 = ml[3 * kTile + row];
+      const float mm = fmaxf(m0, m1);
+      w0 = ex2_approx(m0 - mm);
+      w1 = ex2_approx(m1 - mm);
+      l_run = l0 * w0 + l1 * w1;
     }
   }
-  // O columns [col, col + 32) of this thread's row, merged (KS) in place.
-  auto merge_o = [&](uint32_t (&o)[32], uint32_t col) {
-    if constexpr (KS) {
-      if (has1) {
-        uint32_t o1[32];
-        if constexpr (LS)  // tile 1's accumulator, this thread's half row
-          tmem_ld16x2(tO + DB * kTile + col, o1);
-        else
-          tmem_ld32(tO + DB * kTile + col, o1);  // tile 1's accumulator
-        tmem_wait_ld();
-        reg_fence(o1);
+  // Accumulator columns [col, col + 32) of this thread's row (KS: tile 0's,
+  // merged in place with tile 1's, both loads in flight together).
+  const uint32_t tOe = KS ? tmem + lane_base + NQ * kTile : tO;
+  auto load_o = [&](uint32_t (&o)[32], uint32_t col) {
+    uint32_t o1[32];
+    if constexpr (LS)
+      tmem_ld16x2(tOe + col, o);
+    else
+      tmem_ld32(tOe + col, o);
+    if (KS && has1) {
+      if constexpr (LS)  // tile 1's accumulator, this thread's half row
+        tmem_ld16x2(tOe + DB * kTile + col, o1);
+      else
+        tmem_ld32(tOe + DB * kTile + col, o1);
+    }
+    tmem_wait_ld();
+    reg_fence(o);
+    if (KS && has1) {
+      reg_fence(o1);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          o[i] = __float_as_uint(
-              __fmaf_rn(__uint_as_float(o[i]), w0, __fmul_rn(__uint_as_float(o1[i]), w1)));
-      }
+      for (int i = 0; i < 32; ++i)
+        o[i] = __float_as_uint(
+            __fmaf_rn(__uint_as_float(o[i]), w0, __fmul_rn(__uint_as_float(o1[i]), w1)));
     }
   };
   if (tracer) RP_TRACE(204 + t, 0);  // last PV done: epilogue starts
 
   // Epilogue: O * (sv_max / 448) / l -> bf16 or fp16, staged in this tile's
-  // (now idle) Q and P buffers and written by TMA: 2 DB boxes of 64 columns
-  // in the 128-byte swizzle, or (out_plain, D <= 64) one unswizzled box of D.
+  // (now idle) Q and P buffers (KS: tile 0's) and written by TMA: 2 DB boxes
+  // of 64 columns in the 128-byte swizzle, or (out_plain, D <= 64) one
+  // unswizzled box of D.
   tc_fence_after();
   const float f = (sv_max / 448.f) / l_run;
+  const int ts = KS ? 0 : t;
+  uint8_t* const pbase_e = smem + C::kOffP + ts * C::kPBuf * C::kPStride;
   auto stage_of = [&](int box) -> uint8_t* {
-    return (box & 1) ? pbase + (box >> 1) * kTileBytes
-                     : smem + C::kOffQ + t * C::kQBytes + (box >> 1) * kTileBytes;
+    return (box & 1) ? pbase_e + (box >> 1) * kTileBytes
+                     : smem + C::kOffQ + ts * C::kQBytes + (box >> 1) * kTileBytes;
   };
   auto pack2 = [&](float a, float b) -> uint32_t {
     return p.out_f16 ? pack_half2(a * f, b * f) : pack_bf16x2(a * f, b * f);
@@ -1062,10 +1133,7 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
     for (int cc = 0; cc < 2; ++cc) {
       if (cc * 32 < ncols) {
         uint32_t o[32];
-        tmem_ld32(tO + 32 * cc, o);
-        tmem_wait_ld();
-        reg_fence(o);
-        merge_o(o, 32 * cc);
+        load_o(o, 32 * cc);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float* v = reinterpret_cast<const float*>(o) + 8 * q;
@@ -1082,14 +1150,10 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
       const uint32_t srow = smem_u32(stage_of(box)) + row * 128;
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
+        if (KS && cc != t) continue;  // the other warpgroup's half
         uint32_t o[32];
-        if constexpr (LS)
-          tmem_ld16x2(tO + 32 * cc, o);  // the thread's own 64-column half, 32 at a time
-        else
-          tmem_ld32(tO + 64 * hh + 32 * cc, o);
-        tmem_wait_ld();
-        reg_fence(o);
-        merge_o(o, 64 * hh + 32 * cc);
+        // LS: the thread's own 64-column half, 32 at a time
+        load_o(o, LS ? 32 * cc : 64 * hh + 32 * cc);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int k = cc * 4 + q;
@@ -1102,9 +1166,14 @@ __device__ void softmax_wg(const CUtensorMap* tm_o, const AttnKernelParams& p, c
   }
   fence_proxy_async_smem();
   __syncwarp();
-  if (lane == 0) mbar_arrive(bar.epi + t);
-  if (wq == 0 && lane == 0 && half == 0 && q_tile < p.n_q_tiles) {
-    if (mbar_wait(bar.epi + t, 0, bar.abort_flag, p.status, kErrWaitEpi)) {
+  if (tracer) RP_TRACE(218 + t, 0);  // this warp's part of the output staged
+  if (lane == 0) mbar_arrive(KS ? bar.epi2 + t : bar.epi + t);
+  if (wq == 0 && lane == 0 && half == 0 && (!KS || t == 0) && q_tile < p.n_q_tiles) {
+    const bool staged =
+        KS ? mbar_wait(bar.epi2, 0, bar.abort_flag, p.status, kErrWaitEpi) &&
+                 mbar_wait(bar.epi2 + 1, 0, bar.abort_flag, p.status, kErrWaitEpi)
+           : mbar_wait(bar.epi + t, 0, bar.abort_flag, p.status, kErrWaitEpi);
+    if (staged) {
       const int b = bh / p.H, h = bh % p.H;
       if (NSPLIT == 1 && p.out_plain) {
         tma_store_4d(tm_o, stage_of(0), 0, q_tile * kTile, h, b);
@@ -1136,29 +1205,21 @@ __global__ void __launch_bounds__(Cfg<NQ, PMODE, NSPLIT>::kThreads, 1)
   RP_TRACE_INIT();
   if (threadIdx.x == 0) RP_TRACE(200, 0);  // kernel entry
 
-  if (threadIdx.x == 0) {
-    mbar_init(bar.q_full, 1);
-    for (int i = 0; i < kKSt; ++i) {
-      mbar_init(bar.k_full + i, 1);
-      mbar_init(bar.k_empty + i, 1);
+  if (warp == 0) {
+    // The barriers lie back to back from q_full (carve_bars); one lane
+    // initialises every 32nd.  Arrival counts: one per softmax warp of a tile
+    // for s_free, p_full, epi and epi2, two for the row-max exchange, else one.
+    for (int i = lane; i < C::kNumBars; i += 32) {
+      uint64_t* b = bar.q_full + i;
+      uint32_t count = 1;
+      if ((b >= bar.s_free && b < bar.o_done) || (b >= bar.epi && b < bar.fin) ||
+          (b >= bar.epi2 && b < bar.epi2 + NQ))
+        count = C::kWarpsPerTile;
+      else if (b >= bar.xch && b < bar.stag)
+        count = 2;
+      mbar_init(b, count);
     }
-    for (int i = 0; i < kVSt; ++i) {
-      mbar_init(bar.v_full + i, 1);
-      mbar_init(bar.v_empty + i, 1);
-    }
-    for (int t = 0; t < NQ; ++t) {
-      mbar_init(bar.s_full + t, 1);
-      mbar_init(bar.s_free + t, C::kWarpsPerTile);
-      mbar_init(bar.p_full + 2 * t, C::kWarpsPerTile);
-      mbar_init(bar.p_full + 2 * t + 1, C::kWarpsPerTile);
-      mbar_init(bar.o_done + t, 1);
-      mbar_init(bar.o_final + t, 1);
-      mbar_init(bar.epi + t, C::kWarpsPerTile);
-    }
-    mbar_init(bar.fin, 1);
-    for (int i = 0; i < 12 * NQ; ++i) mbar_init(bar.xch + i, 2);
-    for (int i = 0; i < 32; ++i) mbar_init(bar.stag + i, 1);
-    *bar.abort_flag = 0;
+    if (lane == 0) *bar.abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == C::kMmaWarp) {
