@@ -736,6 +736,9 @@ def dominant_roofline(w: dict, runner: Runner, kernel_ms: float, peaks: dict) ->
             "kernel": "fa8_fwd_kernel<2,%d>" % runner.args.p_mode}
 
 
+DECODE_SETTLE_S = 1.0  # idle seconds between the timed region and the decode record
+
+
 def decode_record(args, dev, stream, peaks: dict) -> dict:  # type: ignore[no-untyped-def]
     """The shared-prefix decode (token-VLA config) on this GPU, outside the
     timed region: one decode step (quantize the new queries and suffix K/V,
@@ -971,12 +974,25 @@ def run_b200_arm(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     ms_step = ms_total / args.steps
     value = runner.job_flops * args.steps / (ms_total / 1e3) / 1e12
 
-    side = side_measurements(runner, dev, stream, load_peaks()) if world == 1 and not args.no_side else {}
+    decode = None
     if world == 1 and not args.no_side and w["kind"] != "decode":
+        # The decode is latency-bound and sensitive to the SM clock: right after seconds
+        # of power-capped work (the side rows' GEMMs) it ran ~50 % slower on B200 until
+        # the clocks recovered, so it runs before them, after a short idle, with its own
+        # clock samples.
+        time.sleep(DECODE_SETTLE_S)
+        dec_clock = ClockSampler(local_rank)
+        dec_clock.start()
+        time.sleep(0.3)  # the sampler's first reading lands inside the measurement
         try:
-            side["decode"] = decode_record(args, dev, stream, load_peaks())
+            decode = decode_record(args, dev, stream, load_peaks())
         except Exception as e:  # a failure here must not hide the headline line
-            side["decode"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+            decode = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        decode["clocks"] = dec_clock.stop()
+        decode["settle_s"] = DECODE_SETTLE_S
+    side = side_measurements(runner, dev, stream, load_peaks()) if world == 1 and not args.no_side else {}
+    if decode is not None:
+        side["decode"] = decode
 
     e2e = None
     if not args.no_e2e:
