@@ -191,6 +191,7 @@ class ContextParallelAttention:
         self.scale = scale
         self.scale_mode = scale_mode
         self.all_reduce_max = all_reduce_max
+        self._streams: dict = {}  # device index -> chunk streams (attend_quantized)
         if scale_mode == 0 and world > 1 and all_reduce_max is None:
             raise ValueError("per-(b,h) scales over several ranks need all_reduce_max")
 
@@ -351,7 +352,11 @@ class ContextParallelAttention:
         When the bound all_gather is asynchronous the (b, h) range is cut into
         chunks -- ``cp_chunk_bounds``'s plan by default, or ``chunks`` even
         parts -- every chunk's gathers are issued first, and chunk i's
-        attention waits only for chunk i's gathers."""
+        attention waits only for chunk i's gathers.  Each chunk's launch goes
+        on a stream of its own (after the calling stream's work and its
+        gathers), and the calling stream waits for all of them at the end: a
+        chunk's CTAs then take the SMs that the previous chunk's last CTAs
+        free, instead of waiting for that whole launch to finish."""
         import torch
 
         from repercep_runtime_b200 import ops
@@ -363,7 +368,7 @@ class ContextParallelAttention:
         v8 = vq.data.view(torch.uint8).reshape(bh, rows, D)
         if chunks is None:
             sms = torch.cuda.get_device_properties(qq.data.device).multi_processor_count
-            bounds = cp_chunk_bounds(bh, -(-rows // BLOCK), sms)
+            bounds = self.chunk_plan(bh, sms)
         else:
             n = max(1, min(chunks, bh))
             bounds = [(i * bh // n, (i + 1) * bh // n) for i in range(n)]
@@ -383,15 +388,41 @@ class ContextParallelAttention:
         q4 = qq.data.reshape(1, bh, rows, qq.data.shape[-1])
         qs = qq.scales.reshape(bh, -1)
         o4 = out.view(1, bh, rows, D)
-        for (a, b), (k_all, v_all, sc_all, works) in zip(bounds, pending):
-            for w in works:
-                w.wait()
-            qc = ops.Quantized(q4[:, a:b], qs[a:b], ops.SCALE_PER_BLOCK128, d=qq.d)
-            ops.attention_fp8_chunked(qc, k_all.view(ops.FP8), v_all.view(ops.FP8),
-                                      sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous(),
-                                      last_rows=sh.last_rows, scale=self.scale, p_mode=self.p_mode,
-                                      out=o4[:, a:b])
+        caller = torch.cuda.current_stream(out.device)
+        streams = self._chunk_streams(out.device, len(bounds))
+        done = []
+        for s, (a, b), (k_all, v_all, sc_all, works) in zip(streams, bounds, pending):
+            s.wait_stream(caller)  # Q, the output and the gather buffers come from the caller's stream
+            with torch.cuda.stream(s):
+                for w in works:
+                    w.wait()  # this chunk's gathers, on this chunk's stream
+                qc = ops.Quantized(q4[:, a:b], qs[a:b], ops.SCALE_PER_BLOCK128, d=qq.d)
+                ops.attention_fp8_chunked(qc, k_all.view(ops.FP8), v_all.view(ops.FP8),
+                                          sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous(),
+                                          last_rows=sh.last_rows, scale=self.scale, p_mode=self.p_mode,
+                                          out=o4[:, a:b])
+                ev = torch.cuda.Event()
+                ev.record(s)
+            done.append(ev)
+        for ev in done:
+            caller.wait_event(ev)
         return out
+
+    def chunk_plan(self, bh: int, sms: int = 148) -> list[tuple[int, int]]:
+        """The (b, h) ranges of the overlapped call.  Every rank must cut the
+        same ranges (each range is one set of collectives), so the plan comes
+        from the shared chunk_rows, not from this rank's own row count, which
+        is shorter on the last rank."""
+        return cp_chunk_bounds(bh, self.shard.chunk_rows // BLOCK, sms)
+
+    def _chunk_streams(self, device, n: int) -> list:  # type: ignore[no-untyped-def]
+        """n streams of this device for the chunk launches, created once."""
+        import torch
+
+        have = self._streams.setdefault(device.index, [])
+        while len(have) < n:
+            have.append(torch.cuda.Stream(device=device))
+        return have[:n]
 
 
 __all__ = [

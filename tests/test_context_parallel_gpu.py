@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import os
 import socket
+import threading
 
 import pytest
 import torch
@@ -115,6 +116,104 @@ def test_per_bh_context_parallel_emulated(S, world):
                                         v_all.view(ops.FP8), ks_all, vs_all, last_rows=shards[0].last_rows)
         torch.cuda.synchronize()
         assert torch.equal(out, ref[:, :, sh.start : sh.start + sh.rows]), f"rank {r}"
+
+
+class _EventWork:
+    """What an asynchronous collective hands back: wait() makes the calling
+    stream wait for the transfer (no host wait)."""
+
+    def __init__(self, ev) -> None:  # type: ignore[no-untyped-def]
+        self.ev = ev
+
+    def wait(self) -> None:
+        torch.cuda.current_stream().wait_event(self.ev)
+
+
+class _ThreadGather:
+    """An asynchronous all_gather_into_tensor for ranks emulated as threads on
+    one GPU.  Each rank publishes its input with an event; after a host
+    barrier every rank copies all inputs into its output, rank-major, on a
+    side stream of its own, and returns a handle whose wait() orders the
+    caller's stream after the copies."""
+
+    def __init__(self, world: int) -> None:
+        self.world = world
+        self.barrier = threading.Barrier(world, timeout=120)
+        self.slots: list = [None] * world
+        self.side: dict = {}
+
+    def for_rank(self, rank: int):  # type: ignore[no-untyped-def]
+        def gather(out, inp, async_op=False):  # type: ignore[no-untyped-def]
+            ev = torch.cuda.Event()
+            ev.record()
+            self.slots[rank] = (inp, ev)
+            self.barrier.wait()
+            side = self.side.setdefault(rank, torch.cuda.Stream())
+            side.wait_stream(torch.cuda.current_stream())
+            parts = out.view(self.world, -1)
+            with torch.cuda.stream(side):
+                for r, (x, e) in enumerate(list(self.slots)):
+                    side.wait_event(e)
+                    parts[r].copy_(x.reshape(-1))
+                    x.record_stream(side)
+                done = torch.cuda.Event()
+                done.record(side)
+            out.record_stream(side)
+            self.barrier.wait()  # every rank has read the slots before any rank refills its own
+            work = _EventWork(done)
+            if async_op:
+                return work
+            work.wait()
+            return None
+
+        gather.supports_async = True  # type: ignore[attr-defined]
+        return gather
+
+
+@pytest.mark.parametrize("S,world,chunks", [(1000, 3, None), (1000, 3, 3), (75600 // 16, 4, 4), (600, 2, None)])
+def test_chunk_streams_with_asynchronous_gathers_emulated(S, world, chunks):
+    """The overlapped path of ContextParallelAttention (every chunk's gathers
+    issued first, each chunk's attention on a stream of its own that waits only
+    for its gathers, the caller's stream joining them all), with the ranks as
+    threads on one GPU and an asynchronous all-gather between them.  Two calls
+    per rank (the chunk streams are reused); every rank's rows equal the
+    single-GPU per-block result bit for bit.  (600, 2): the two ranks' shards
+    have different query-tile counts, and both must still cut the same chunks."""
+    from repercep_runtime_b200.parallel import ContextParallelAttention
+
+    B, H, D = 1, 80 if S == 600 else 4, 128
+    q, k, v = (gen_bf16((B, H, S, D), "n05", 90 + i).cuda() for i in range(3))
+    ref = _single(q, k, v)
+    torch.cuda.synchronize()
+    tg = _ThreadGather(world)
+    outs: list = [None] * world
+    errors: list = []
+
+    def run(rank: int) -> None:
+        try:
+            torch.cuda.set_device(0)
+            with torch.cuda.stream(torch.cuda.Stream()):
+                cp = ContextParallelAttention(S, rank, world, all_gather=tg.for_rank(rank))
+                sh = cp.shard
+                sl = slice(sh.start, sh.start + sh.rows)
+                shards = [t[:, :, sl].contiguous() for t in (q, k, v)]
+                for _ in range(2):
+                    o = cp._device_call(*shards, chunks=chunks)
+                torch.cuda.current_stream().synchronize()
+                outs[rank] = (sl, o)
+        except BaseException as e:  # noqa: BLE001 - reported below
+            errors.append(e)
+            tg.barrier.abort()
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=300)
+    assert not any(th.is_alive() for th in threads), "emulated ranks did not finish"
+    assert not errors, errors
+    for rank, (sl, o) in enumerate(outs):
+        assert torch.equal(o, ref[:, :, sl]), f"rank {rank}"
 
 
 def test_context_parallel_world_one_is_the_plain_call():

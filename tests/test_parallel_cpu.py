@@ -203,3 +203,17 @@ def test_cp_chunk_plan(bh, rows, first, sizes):
     assert [y - x for x, y in b] == sizes
     assert b[0] == (0, first)
     assert b[0][0] == 0 and b[-1][1] == bh and all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
+
+
+@pytest.mark.parametrize("S,world", [(600, 2), (75600, 8), (75600, 7), (1000, 3), (129, 2), (57600, 6)])
+def test_every_rank_cuts_the_same_chunks(S, world):
+    """Each chunk of the overlapped call is one set of collectives, so every
+    rank must plan the same (b, h) ranges -- also the last rank, whose shard
+    is shorter (S = 600 on 2 ranks: 384 and 216 rows, 3 and 2 query tiles)."""
+    from repercep_runtime_b200.parallel import ContextParallelAttention
+
+    for bh in (1, 12, 80, 400):
+        plans = {tuple(ContextParallelAttention(S, r, world).chunk_plan(bh)) for r in range(world)}
+        assert len(plans) == 1, (bh, plans)
+        (plan,) = plans
+        assert plan[0][0] == 0 and plan[-1][1] == bh
