@@ -390,22 +390,24 @@ class ContextParallelAttention:
         o4 = out.view(1, bh, rows, D)
         caller = torch.cuda.current_stream(out.device)
         streams = self._chunk_streams(out.device, len(bounds))
-        done = []
-        for s, (a, b), (k_all, v_all, sc_all, works) in zip(streams, bounds, pending):
-            s.wait_stream(caller)  # Q, the output and the gather buffers come from the caller's stream
-            with torch.cuda.stream(s):
-                for w in works:
-                    w.wait()  # this chunk's gathers, on this chunk's stream
-                qc = ops.Quantized(q4[:, a:b], qs[a:b], ops.SCALE_PER_BLOCK128, d=qq.d)
-                ops.attention_fp8_chunked(qc, k_all.view(ops.FP8), v_all.view(ops.FP8),
-                                          sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous(),
-                                          last_rows=sh.last_rows, scale=self.scale, p_mode=self.p_mode,
-                                          out=o4[:, a:b])
-                ev = torch.cuda.Event()
-                ev.record(s)
-            done.append(ev)
-        for ev in done:
-            caller.wait_event(ev)
+        used = []
+        try:
+            for s, (a, b), (k_all, v_all, sc_all, works) in zip(streams, bounds, pending):
+                s.wait_stream(caller)  # Q, the output and the gather buffers come from the caller's stream
+                used.append(s)
+                with torch.cuda.stream(s):
+                    for w in works:
+                        w.wait()  # this chunk's gathers, on this chunk's stream
+                    qc = ops.Quantized(q4[:, a:b], qs[a:b], ops.SCALE_PER_BLOCK128, d=qq.d)
+                    ops.attention_fp8_chunked(qc, k_all.view(ops.FP8), v_all.view(ops.FP8),
+                                              sc_all[:, 0].contiguous(), sc_all[:, 1].contiguous(),
+                                              last_rows=sh.last_rows, scale=self.scale, p_mode=self.p_mode,
+                                              out=o4[:, a:b])
+        finally:
+            # also when a launch raised: nothing the chunk streams were given
+            # may be reused by the caller's stream before they are done with it
+            for s in used:
+                caller.wait_stream(s)
         return out
 
     def chunk_plan(self, bh: int, sms: int = 148) -> list[tuple[int, int]]:
